@@ -1,0 +1,431 @@
+"""Benchmark: exact L2 k-NN QPS on the headline configuration.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One step = one search batch of Q queries against the whole dataset (row-
+sharded over the N GPUs, one process per GPU under torchrun).  The default
+workload is BASELINE.json's headline: N = 1,000,000 rows, D = 1024, Q = 100,
+K = 10, unit-norm Gaussian mixture (10,000 centres, sigma 0.3).
+
+Printed on rank 0, one JSON line:
+  value        QPS with queries and results resident in HBM (device timing,
+               CUDA events on the launching stream, max over ranks)
+  e2e          QPS through the public API with pinned HOST queries/results,
+               H2D + D2H inside the timed region
+  roofline     the scan kernel's achieved HBM GB/s (algorithmic bytes
+               N_shard * D * 2 per launch / its CUDA-event duration) against
+               MEASURED_PEAKS.json's copy bandwidth
+  cpu_baseline the reference's own CPU exact search (oracle/_ref, compiled
+               from its src/cagra.cpp) on a bounded sample of queries, all
+               host threads; plus an OpenBLAS expanded-form port
+  clocks       SM clock samples (NVML) during the timed region
+
+--impl reference times the reference's CPU implementation alone (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "cuvs-silicon_b200")
+
+METRIC = "QPS at N=1M D=1024 K=10 Q=100 (1/2/4/8 B200) and % of HBM/tensor roofline"
+UNIT = "queries/s"
+PUBLISHED_QPS = 1012.0  # reference README.md:23-27, Apple M3 Max
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--n", type=int, default=1_000_000)
+    ap.add_argument("--dim", type=int, default=1024)
+    ap.add_argument("--q", type=int, default=100)
+    ap.add_argument("--k", type=int, default=10)
+    ap.add_argument("--centres", type=int, default=10_000)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    a = ap.parse_args()
+    a.warmup = max(a.warmup, 3)
+    return a
+
+
+def workload_name(a):
+    head = (a.n, a.dim, a.q, a.k) == (1_000_000, 1024, 100, 10)
+    return ("headline " if head else "") + f"N={a.n} D={a.dim} Q={a.q} K={a.k}"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic(a, n_shard):
+    """dram bytes per scan launch from the committed ncu summary, scaled to
+    this shard's rows when it was captured on a different row count."""
+    path = os.path.join(ROOT, "profiles", "knn_scan_headline.md")
+    try:
+        vals = {}
+        for line in open(path):
+            if ":" in line and line.strip().startswith("- "):
+                key, _, v = line.strip()[2:].partition(":")
+                vals[key.strip()] = v.strip().split()[0]
+        t = float(vals["traffic_bytes_per_launch"])
+        rows = float(vals["captured_rows"])
+        if int(vals.get("captured_dim", a.dim)) != a.dim:
+            return None
+        return t * n_shard / rows
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """Samples the SM clock and throttle reasons through NVML (read only)."""
+
+    def __init__(self, device_index: int):
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+        self.names = {}
+        if self.nv:
+            for n in ("GpuIdle", "ApplicationsClocksSetting", "SwPowerCap", "HwSlowdown",
+                      "SyncBoost", "SwThermalSlowdown", "HwThermalSlowdown",
+                      "HwPowerBrakeSlowdown", "DisplayClockSetting"):
+                v = getattr(self.nv, "nvmlClocksEventReason" + n, None)
+                if v is None:
+                    v = getattr(self.nv, "nvmlClocksThrottleReason" + n, None)
+                if v is not None:
+                    self.names[v] = n
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                try:
+                    r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                except Exception:
+                    r = self.nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+                for bit, name in self.names.items():
+                    if r & bit and name != "GpuIdle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self.nv:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self.nv:
+            self.t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def gen_mixture_device(torch, n_total, begin, end, dim, centres, seed, device, sigma=0.3):
+    """Rows [begin, end) of the unit-norm mixture, generated on the GPU in
+    65,536-row chunks; chunk c uses generator seed (seed, c), so every rank
+    reproduces its own row shard without materialising the others."""
+    chunk = 65536
+    out = torch.empty((end - begin, dim), dtype=torch.float32, device=device)
+    c0, c1 = begin // chunk, (end - 1) // chunk if end > begin else -1
+    for c in range(c0, c1 + 1):
+        lo, hi = c * chunk, min(n_total, (c + 1) * chunk)
+        g = torch.Generator(device=device)
+        g.manual_seed(seed * 1_000_003 + c)
+        u = torch.randint(0, centres.shape[0], (hi - lo,), generator=g, device=device)
+        x = torch.randn((hi - lo, dim), generator=g, device=device)
+        x.mul_(sigma).add_(centres[u])
+        x.div_(x.norm(dim=1, keepdim=True))
+        a, b = max(lo, begin), min(hi, end)
+        out[a - begin:b - begin] = x[a - lo:b - lo]
+    return out
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_reference_qps(base16_host, q16_host, k, sample_q, threads):
+    """The reference's own exact CPU search (oracle/_ref) on sample_q queries
+    against every row; returns (qps, seconds, idx)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    q = q16_host[:sample_q]
+    use_ref = oracle.ref_available()
+    t0 = time.perf_counter()
+    if use_ref:
+        idx, dist = oracle.ref_knn(base16_host, q, k, threads=threads)
+    else:
+        idx, dist = oracle.port_knn(base16_host, q, k, threads=threads)
+    dt = time.perf_counter() - t0
+    return sample_q / dt, dt, idx, dist, ("reference" if use_ref else "port")
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+
+    import oracle
+
+    threads = host_threads()
+    centres = oracle.gen_centres(a.centres, a.dim)
+    base = oracle.round_fp16(oracle.gen_mixture(a.n, a.dim, a.centres, oracle.SEED_BASE,
+                                                centres=centres, threads=threads))
+    queries = oracle.round_fp16(oracle.gen_mixture(a.q, a.dim, a.centres,
+                                                   oracle.SEED_QUERIES, centres=centres))
+    kind = "reference" if oracle.ref_available() else "port"
+    fn = oracle.ref_knn if kind == "reference" else oracle.port_knn
+    # one step = a bounded sample of the batch: one query per host thread
+    sample = max(1, min(a.q, threads))
+    times = []
+    for s in range(a.warmup + a.steps):
+        lo = (s * sample) % a.q
+        q = np.roll(queries, -lo, axis=0)[:sample]
+        t0 = time.perf_counter()
+        fn(base, q, a.k, threads=threads)
+        dt = time.perf_counter() - t0
+        if s >= a.warmup:
+            times.append(dt)
+    total = sum(times)
+    qps = sample * len(times) / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": qps, "unit": UNIT,
+        "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": 1000.0 * total / len(times), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": qps / PUBLISHED_QPS, "dtype": "f32",
+        "data": "synthetic: unit-norm Gaussian mixture (numpy PCG64, seeds 11/12/13), "
+                "fp16-rounded, fp32 on host",
+        "config": {"workload": workload_name(a), "n_rows": a.n, "dim": a.dim,
+                   "n_queries": a.q, "k": a.k,
+                   "sample": f"{sample} queries per step x all {a.n} rows"},
+        "cpu_baseline": {"value": qps, "unit": UNIT, "cores": min(threads, sample),
+                         "kind": kind,
+                         "sample": f"{sample} of {a.q} queries per step against all rows"},
+        "e2e": {"value": qps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- engine arm
+def run_engine(a):
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, PKG)
+    import cuvs_b200 as E
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    # ---- data (synthetic, on device)
+    cg = torch.Generator(device=dev)
+    cg.manual_seed(11)
+    centres = torch.randn((a.centres, a.dim), generator=cg, device=dev)
+    lo, hi = E.shard_range(a.n, world, rank)
+    shard = gen_mixture_device(torch, a.n, lo, hi, a.dim, centres, 12, dev)
+    queries = gen_mixture_device(torch, a.q, 0, a.q, a.dim, centres, 13, dev)
+
+    idx = E.Index(local)
+    stream = torch.cuda.current_stream()
+    idx.set_stream(stream.cuda_stream)
+    idx.build(shard, row_offset=lo, total_rows=a.n)
+    torch.cuda.synchronize()
+    host_base16 = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        host_base16 = shard.half().float().cpu().numpy()
+    del shard
+    if world > 1:
+        obj = [E.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        idx.attach_comm(obj[0], world, rank)
+
+    out_i = torch.empty((a.q, a.k), dtype=torch.int32, device=dev)
+    out_d = torch.empty((a.q, a.k), dtype=torch.float32, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- warm-up
+    for _ in range(a.warmup):
+        idx.search_async(queries, a.k, out_i, out_d)
+    idx.sync()
+
+    # ---- device-resident timing (value)
+    clk = ClockSampler(local)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    idx.reset_kernel_stats()
+    barrier()
+    with clk:
+        ev0.record(stream)
+        for _ in range(a.steps):
+            idx.search_async(queries, a.k, out_i, out_d)
+        ev1.record(stream)
+        idx.sync()
+        torch.cuda.synchronize()
+    dev_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    launches = idx.kernel_stats()["kernel_launches"]
+    launches_total = int(max_over_ranks(float(launches)) * world)
+    value = a.q * a.steps / (dev_ms / 1000.0)
+
+    # ---- kernel timing for the roofline (events around the scan kernel)
+    idx.set_profiling(True)
+    idx.reset_kernel_stats()
+    barrier()
+    for _ in range(a.steps):
+        idx.search_async(queries, a.k, out_i, out_d)
+    idx.sync()
+    st = idx.kernel_stats()
+    idx.set_profiling(False)
+    scan_ms = max_over_ranks(st["scan_ms"] / max(1, st["scan_launches"]))
+    merge_ms = max_over_ranks(st["merge_ms"] / max(1, st["scan_launches"]))
+
+    # ---- end-to-end through the public API with pinned host buffers
+    q_host = queries.cpu().pin_memory()
+    i_host = torch.empty((a.q, a.k), dtype=torch.int32).pin_memory()
+    d_host = torch.empty((a.q, a.k), dtype=torch.float32).pin_memory()
+    for _ in range(3):
+        idx.search(q_host, a.k, neighbors=i_host, distances=d_host)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(a.steps):
+        idx.search(q_host, a.k, neighbors=i_host, distances=d_host)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e = a.q * a.steps / (e2e_ms / 1000.0)
+    gpu_nbrs = i_host.numpy().view("uint32").copy()
+
+    # ---- CPU baselines (rank 0, N = 1 only; bounded samples)
+    cpu = None
+    extra = {}
+    if host_base16 is not None:
+        threads = host_threads()
+        q16 = queries.half().float().cpu().numpy()
+        sample = max(1, min(a.q, 2 * threads))
+        qps, secs, ref_i, ref_d, kind = cpu_reference_qps(host_base16, q16, a.k, sample, threads)
+        cpu = {"value": qps, "unit": UNIT, "cores": min(threads, sample), "kind": kind,
+               "sample": f"{sample} of {a.q} queries against all {a.n} rows "
+                         f"({secs:.1f} s, reference cagra::search, one query slice per thread)"}
+        hits = sum(len(set(x.tolist()) & set(y.tolist()))
+                   for x, y in zip(gpu_nbrs[:sample], ref_i))
+        extra["recall_vs_reference_sample"] = hits / float(ref_i.size)
+        try:
+            sys.path.insert(0, os.path.join(ROOT, "oracle"))
+            import oracle
+
+            t0 = time.perf_counter()
+            oracle.blas_knn(host_base16, q16, a.k)
+            bt = time.perf_counter() - t0
+            extra["cpu_blas_expanded_form"] = {
+                "value": a.q / bt, "unit": UNIT, "cores": threads, "kind": "port",
+                "sample": f"all {a.q} queries, numpy float32 matmul "
+                          f"(OpenBLAS sgemm, {oracle.blas_threads()}), {bt:.1f} s"}
+        except Exception as e:  # informational only
+            extra["cpu_blas_expanded_form"] = {"error": str(e)[:200]}
+
+    n_shard = hi - lo
+    peak, peak_kind = peaks()
+    achieved = (n_shard * a.dim * 2) / (scan_ms / 1000.0) / 1e9
+    traffic = profile_traffic(a, n_shard)
+    shard_mb = n_shard * a.dim * 2 / 2 ** 20
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": dev_ms / a.steps,
+            "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": value / PUBLISHED_QPS, "dtype": "f16",
+            "data": "synthetic: unit-norm Gaussian mixture (10,000 centres, sigma 0.3), "
+                    "generated on device with torch (seeds 11/12/13)",
+            "config": {"workload": workload_name(a), "n_rows": a.n, "dim": a.dim,
+                       "n_queries": a.q, "k": a.k,
+                       "parallelism": f"row-shard x{world}" + (" + NCCL all-gather"
+                                                               if world > 1 else ""),
+                       "l2": f"inputs larger than L2 (dataset shard {shard_mb:.0f} MiB "
+                             f"> 126 MiB), no flush"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_kind": peak_kind, "kernel": "knn_scan_kernel",
+                         "kernel_ms": scan_ms, "merge_ms": merge_ms,
+                         "algorithmic_bytes_per_launch": n_shard * a.dim * 2},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": a.q * a.dim * 4,
+                    "d2h_bytes_per_step": a.q * a.k * 8},
+            "gpu_launches": launches_total,
+            "clocks": clk.summary(),
+        }
+        line.update(extra)
+        print(json.dumps(line), flush=True)
+    idx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        return run_reference(a)
+    return run_engine(a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

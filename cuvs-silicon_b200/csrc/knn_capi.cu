@@ -1,0 +1,747 @@
+// knn_capi.cu -- the engine behind include/cuvs_b200.h.
+//
+// Host orchestration of the exact search, replacing
+// MetalContext::search_brute_force (src/metal_context.mm:139-255):
+//
+//   reference (per call)                      this engine
+//   -------------------------------------     ------------------------------------
+//   first call: fp16 dataset + d_norms on     knn_index_build: rows -> HBM fp16
+//     one CPU thread, cached by (ptr,N,D)       (ld-padded) + norms, one kernel
+//   Q x D fp16 + q_norms on the host          queries -> device, convert kernel
+//   MPS GEMM -> Q x N fp32 in memory          fused scan kernel (TMA + tcgen05),
+//   l2_topk_from_cross (K <= 16)                Q x N stays on chip, any k<=512
+//   copy Q x K out                            merge kernel -> caller's buffers
+//
+// Multi-GPU: one process per GPU, each index holds a contiguous row shard;
+// the per-rank top-k lists are all-gathered with NCCL and merged on every
+// rank.  NCCL is created non-blocking and every wait on it is bounded by a
+// host deadline, after which the communicator is aborted (KNN_ENCCL).
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <type_traits>
+
+#include "../../include/cuvs_b200.h"
+#include "knn_internal.h"
+
+using knn::Plan;
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<uint64_t> g_dispatch{0};
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+#define KNN_CUDA(call)                                                                   \
+  do {                                                                                   \
+    cudaError_t e_ = (call);                                                             \
+    if (e_ != cudaSuccess)                                                               \
+      return fail(e_ == cudaErrorMemoryAllocation ? KNN_ENOMEM : KNN_ECUDA, "%s: %s (%s)", \
+                  #call, cudaGetErrorString(e_), cudaGetErrorName(e_));                  \
+  } while (0)
+
+// Device buffer that only grows.
+struct DevBuf {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  int ensure(size_t need) {
+    if (need <= bytes) return KNN_OK;
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    bytes = 0;
+    const size_t want = need + need / 4;
+    cudaError_t e = cudaMalloc(&ptr, want);
+    if (e != cudaSuccess) {
+      ptr = nullptr;
+      return fail(KNN_ENOMEM, "cudaMalloc(%zu) failed: %s", want, cudaGetErrorString(e));
+    }
+    bytes = want;
+    return KNN_OK;
+  }
+  void release() {
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    bytes = 0;
+  }
+  template <typename T>
+  T* as() const {
+    return static_cast<T*>(ptr);
+  }
+};
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// K-major fp16 matrix [rows][ld] as a TMA map with 64 x box_rows boxes and
+// 128-byte swizzle.
+int encode_rows(CUtensorMap* map, const __half* base, int64_t rows, int64_t ld,
+                uint32_t box_rows) {
+  auto enc = get_encode();
+  if (!enc) return fail(KNN_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (ld * 2) % 16 != 0)
+    return fail(KNN_ECUDA, "TMA base/stride not 16-byte aligned");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(ld), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(knn::kKChunk), box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(KNN_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return KNN_OK;
+}
+
+int64_t row_ld(int64_t dim) {
+  if (dim < knn::kKChunk) return knn::kKChunk;
+  return (dim + 7) / 8 * 8;
+}
+
+// 0 = host memory, 1 = device memory of `device`, -1 = other device.
+int classify(const void* p, int device) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged)
+    return a.device == device ? 1 : -1;
+  return 0;
+}
+
+
+// NCCL is resolved at run time, the first time a communicator is needed.
+// dlopen("libnccl.so.2") returns the copy the process already holds (for
+// example the one a framework loaded) or else the system library, so the
+// engine never forces a second NCCL version into a process.
+struct NcclApi {
+  bool ok = false;
+  std::string why;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) =
+      nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+const NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      api.why = dlerror();
+      return;
+    }
+    bool all = true;
+    auto get = [&](auto& fn, const char* name) {
+      fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
+      if (!fn) all = false;
+    };
+    get(api.GetUniqueId, "ncclGetUniqueId");
+    get(api.CommInitRankConfig, "ncclCommInitRankConfig");
+    get(api.CommGetAsyncError, "ncclCommGetAsyncError");
+    get(api.CommAbort, "ncclCommAbort");
+    get(api.CommDestroy, "ncclCommDestroy");
+    get(api.AllGather, "ncclAllGather");
+    get(api.GetErrorString, "ncclGetErrorString");
+    api.ok = all;
+    if (!all) api.why = "libnccl.so.2 lacks a required symbol";
+  });
+  return api;
+}
+
+const char* nccl_str(ncclResult_t r) {
+  return nccl().GetErrorString ? nccl().GetErrorString(r) : "nccl unavailable";
+}
+
+}  // namespace
+
+struct knn_index {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+
+  // dataset (this rank's shard)
+  int64_t n = 0, dim = 0, ld = 0;
+  int64_t row_offset = 0, total_rows = 0;
+  int metric = KNN_METRIC_L2_EXPANDED;
+  __half* data = nullptr;
+  float* norms = nullptr;
+  CUtensorMap xmap;
+
+  // per-search scratch
+  DevBuf q32, q16, qnorm, part_d, part_i, out_d, out_i, gather_send, gather_recv;
+  int* err_dev = nullptr;
+  int* err_host = nullptr;  // pinned
+
+  // multi-GPU
+  ncclComm_t comm = nullptr;
+  int n_ranks = 1, rank = 0;
+
+  // profiling
+  bool profiling = false;
+  cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+  double scan_ms = 0.0, merge_ms = 0.0;
+  int64_t scan_launches = 0, kernel_launches = 0;
+};
+
+namespace {
+
+int poll_nccl(knn_index* h, double seconds) {
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    ncclResult_t st = ncclSuccess;
+    ncclResult_t r = nccl().CommGetAsyncError(h->comm, &st);
+    if (r != ncclSuccess) return fail(KNN_ENCCL, "ncclCommGetAsyncError: %s", nccl_str(r));
+    if (st == ncclSuccess) return KNN_OK;
+    if (st != ncclInProgress) {
+      nccl().CommAbort(h->comm);
+      h->comm = nullptr;
+      return fail(KNN_ENCCL, "NCCL async error: %s", nccl_str(st));
+    }
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > seconds) {
+      nccl().CommAbort(h->comm);
+      h->comm = nullptr;
+      return fail(KNN_ENCCL, "NCCL operation did not complete within %.0f s", seconds);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+// Waits for the index stream; with a communicator attached the wait is a
+// poll bounded by a deadline so a lost peer cannot hang the caller.
+int sync_stream(knn_index* h) {
+  if (!h->comm) {
+    KNN_CUDA(cudaStreamSynchronize(h->stream));
+    return KNN_OK;
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    cudaError_t e = cudaStreamQuery(h->stream);
+    if (e == cudaSuccess) return KNN_OK;
+    if (e != cudaErrorNotReady) return fail(KNN_ECUDA, "stream: %s", cudaGetErrorString(e));
+    ncclResult_t st = ncclSuccess;
+    nccl().CommGetAsyncError(h->comm, &st);
+    if (st != ncclSuccess && st != ncclInProgress) {
+      nccl().CommAbort(h->comm);
+      h->comm = nullptr;
+      return fail(KNN_ENCCL, "NCCL async error: %s", nccl_str(st));
+    }
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > 60.0) {
+      nccl().CommAbort(h->comm);
+      h->comm = nullptr;
+      return fail(KNN_ENCCL, "search on the communicator did not complete within 60 s");
+    }
+    std::this_thread::yield();
+  }
+}
+
+int check_device_error(knn_index* h) {
+  if (*h->err_host != 0) {
+    const int code = *h->err_host;
+    *h->err_host = 0;
+    cudaMemsetAsync(h->err_dev, 0, sizeof(int), h->stream);
+    cudaStreamSynchronize(h->stream);
+    return fail(KNN_ETIMEOUT, "scan kernel gave up on a bounded wait (device code %d)", code);
+  }
+  return KNN_OK;
+}
+
+int validate_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
+                    const void* neighbors, const float* distances) {
+  if (!h) return fail(KNN_EINVAL, "null index");
+  if (nq < 0 || k < 0) return fail(KNN_EINVAL, "negative n_queries or k");
+  if (nq == 0 || k == 0) return KNN_OK;
+  // reference: src/cagra.cpp:100-103
+  if (!queries || !neighbors || !distances)
+    return fail(KNN_EINVAL, "search requires valid query and output buffers");
+  if (!h->data) return fail(KNN_EINVAL, "index has no dataset (build it first)");
+  if (k > KNN_MAX_K) return fail(KNN_EUNSUPPORTED, "k = %lld exceeds the maximum %d",
+                                 (long long)k, KNN_MAX_K);
+  return KNN_OK;
+}
+
+// Core search.  out_i64: neighbours are int64.  sync: block and check.
+int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void* neighbors,
+                float* distances, bool out_i64, bool sync, bool require_device) {
+  int st = validate_search(h, queries, nq, k, neighbors, distances);
+  if (st != KNN_OK || nq == 0 || k == 0) return st;
+  std::lock_guard<std::mutex> lock(h->mu);
+  KNN_CUDA(cudaSetDevice(h->device));
+
+  const int cq = classify(queries, h->device);
+  const int cn = classify(neighbors, h->device);
+  const int cd = classify(distances, h->device);
+  if (cq < 0 || cn < 0 || cd < 0)
+    return fail(KNN_EINVAL, "buffer lives on a different device than the index");
+  if (require_device && (cq == 0 || cn == 0 || cd == 0))
+    return fail(KNN_EINVAL, "knn_index_search_async requires device buffers");
+
+  Plan plan;
+  const int pst = knn::plan_search(h->n, h->dim, nq, k, h->num_sms, &plan);
+  if (pst != 0) return fail(pst, "k = %lld is outside the engine's limits", (long long)k);
+
+  // scratch
+  const size_t qk = static_cast<size_t>(nq) * k;
+  if ((st = h->q16.ensure(static_cast<size_t>(nq) * h->ld * 2)) != KNN_OK) return st;
+  if ((st = h->qnorm.ensure(static_cast<size_t>(nq) * 4)) != KNN_OK) return st;
+  if ((st = h->part_d.ensure(static_cast<size_t>(plan.partial_bytes / 2))) != KNN_OK) return st;
+  if ((st = h->part_i.ensure(static_cast<size_t>(plan.partial_bytes / 2))) != KNN_OK) return st;
+
+  const float* qsrc = queries;
+  if (cq == 0) {
+    if ((st = h->q32.ensure(static_cast<size_t>(nq) * h->dim * 4)) != KNN_OK) return st;
+    KNN_CUDA(cudaMemcpyAsync(h->q32.ptr, queries, static_cast<size_t>(nq) * h->dim * 4,
+                             cudaMemcpyHostToDevice, h->stream));
+    qsrc = h->q32.as<float>();
+  }
+  KNN_CUDA(knn::launch_convert_rows(qsrc, false, nq, h->dim, h->q16.as<__half>(), h->ld,
+                                    h->qnorm.as<float>(), h->stream));
+
+  CUtensorMap qmap;
+  if ((st = encode_rows(&qmap, h->q16.as<__half>(), nq, h->ld, knn::kQueryRows)) != KNN_OK)
+    return st;
+
+  knn::ScanParams p;
+  p.row_norms = h->norms;
+  p.query_norms = h->qnorm.as<float>();
+  p.part_d = h->part_d.as<float>();
+  p.part_i = h->part_i.as<uint32_t>();
+  p.err = h->err_dev;
+  p.n_rows = h->n;
+  p.n_queries = nq;
+  p.row_tiles = plan.row_tiles;
+  p.k = static_cast<int32_t>(k);
+  p.query_block = static_cast<int32_t>(plan.query_block);
+  p.query_tiles = static_cast<int32_t>(plan.query_tiles);
+  p.splits = static_cast<int32_t>(plan.splits);
+  p.units = static_cast<int32_t>(plan.units);
+  p.k_chunks = static_cast<int32_t>((h->ld + knn::kKChunk - 1) / knn::kKChunk);
+  p.stages = static_cast<int32_t>(plan.stages);
+  p.dataset_evict_first = plan.query_tiles == 1 ? 1 : 0;
+
+  if (h->profiling) KNN_CUDA(cudaEventRecord(h->ev[0], h->stream));
+  KNN_CUDA(knn::launch_scan(qmap, h->xmap, p, plan, h->stream));
+  if (h->profiling) KNN_CUDA(cudaEventRecord(h->ev[1], h->stream));
+
+  // destination of the merged result
+  const size_t idx_bytes = qk * (out_i64 ? 8 : 4);
+  float* dst_d = distances;
+  void* dst_i = neighbors;
+  if (cd == 0) {
+    if ((st = h->out_d.ensure(qk * 4)) != KNN_OK) return st;
+    dst_d = h->out_d.as<float>();
+  }
+  if (cn == 0) {
+    if ((st = h->out_i.ensure(idx_bytes)) != KNN_OK) return st;
+    dst_i = h->out_i.ptr;
+  }
+
+  int launches = 2;
+  if (!h->comm) {
+    KNN_CUDA(knn::launch_merge(p.part_d, p.part_i, k, plan.splits * k,
+                               static_cast<int>(plan.splits), static_cast<int>(k), nq,
+                               h->row_offset, dst_d, dst_i, out_i64, h->stream));
+    launches += 1;
+  } else {
+    // local merge into the send buffer: [dist k floats | idx k uint32] per query
+    const size_t list_bytes = qk * 8;
+    if ((st = h->gather_send.ensure(list_bytes)) != KNN_OK) return st;
+    if ((st = h->gather_recv.ensure(list_bytes * h->n_ranks)) != KNN_OK) return st;
+    float* send_d = h->gather_send.as<float>();
+    uint32_t* send_i = reinterpret_cast<uint32_t*>(send_d + qk);
+    KNN_CUDA(knn::launch_merge(p.part_d, p.part_i, k, plan.splits * k,
+                               static_cast<int>(plan.splits), static_cast<int>(k), nq,
+                               h->row_offset, send_d, send_i, false, h->stream));
+    ncclResult_t r = nccl().AllGather(h->gather_send.ptr, h->gather_recv.ptr, list_bytes,
+                                   ncclUint8, h->comm, h->stream);
+    if (r == ncclInProgress) {
+      if ((st = poll_nccl(h, 60.0)) != KNN_OK) return st;
+    } else if (r != ncclSuccess) {
+      return fail(KNN_ENCCL, "ncclAllGather: %s", nccl_str(r));
+    }
+    // rank r's block: [qk dist][qk idx]; list l of query q at dist + l*2qk + q*k
+    const float* rd = h->gather_recv.as<float>();
+    const uint32_t* ri = reinterpret_cast<const uint32_t*>(rd + qk);
+    KNN_CUDA(knn::launch_merge(rd, ri, static_cast<int64_t>(2 * qk), k, h->n_ranks,
+                               static_cast<int>(k), nq, 0, dst_d, dst_i, out_i64, h->stream));
+    launches += 2;
+  }
+  if (h->profiling) KNN_CUDA(cudaEventRecord(h->ev[2], h->stream));
+
+  if (cd == 0)
+    KNN_CUDA(cudaMemcpyAsync(distances, dst_d, qk * 4, cudaMemcpyDeviceToHost, h->stream));
+  if (cn == 0)
+    KNN_CUDA(cudaMemcpyAsync(neighbors, dst_i, idx_bytes, cudaMemcpyDeviceToHost, h->stream));
+  g_dispatch.fetch_add(launches);
+  h->kernel_launches += launches;
+  h->scan_launches += 1;
+
+  if (!sync && !h->profiling) return KNN_OK;
+  KNN_CUDA(cudaMemcpyAsync(h->err_host, h->err_dev, sizeof(int), cudaMemcpyDeviceToHost,
+                           h->stream));
+  if ((st = sync_stream(h)) != KNN_OK) return st;
+  if (h->profiling) {
+    float a = 0.f, b = 0.f;
+    KNN_CUDA(cudaEventElapsedTime(&a, h->ev[0], h->ev[1]));
+    KNN_CUDA(cudaEventElapsedTime(&b, h->ev[1], h->ev[2]));
+    h->scan_ms += a;
+    h->merge_ms += b;
+  }
+  return check_device_error(h);
+}
+
+int build_impl(knn_index* h, const void* rows, int dtype, int64_t n, int64_t dim, int metric,
+               int64_t row_offset, int64_t total_rows) {
+  if (!h) return fail(KNN_EINVAL, "null index");
+  // reference: src/cagra.cpp:26-28
+  if (metric != KNN_METRIC_L2_EXPANDED)
+    return fail(KNN_EINVAL, "only the L2Expanded metric is supported");
+  // reference: src/cagra.cpp:29-32
+  if (!rows || n <= 0 || dim <= 0)
+    return fail(KNN_EINVAL, "build requires a non-empty dataset");
+  if (dtype != KNN_DTYPE_F32 && dtype != KNN_DTYPE_F16)
+    return fail(KNN_EINVAL, "unknown dtype %d", dtype);
+  if (row_offset < 0 || total_rows < row_offset + n)
+    return fail(KNN_EINVAL, "shard [%lld, %lld) outside %lld rows", (long long)row_offset,
+                (long long)(row_offset + n), (long long)total_rows);
+  if (total_rows >= static_cast<int64_t>(KNN_NO_INDEX))
+    return fail(KNN_EUNSUPPORTED, "at most 2^32 - 2 rows (uint32 neighbour indices)");
+  if (n > (int64_t(1) << 31) - 256)
+    return fail(KNN_EUNSUPPORTED, "at most 2^31 - 256 rows per device");
+  if (dim > (int64_t(1) << 20)) return fail(KNN_EUNSUPPORTED, "dim above 2^20");
+
+  std::lock_guard<std::mutex> lock(h->mu);
+  KNN_CUDA(cudaSetDevice(h->device));
+  const int where = classify(rows, h->device);
+  if (where < 0) return fail(KNN_EINVAL, "dataset lives on a different device than the index");
+
+  if (h->data) cudaFree(h->data);
+  if (h->norms) cudaFree(h->norms);
+  h->data = nullptr;
+  h->norms = nullptr;
+  h->n = 0;
+
+  const int64_t ld = row_ld(dim);
+  KNN_CUDA(cudaMalloc(&h->data, static_cast<size_t>(n) * ld * 2));
+  KNN_CUDA(cudaMalloc(&h->norms, static_cast<size_t>(n) * 4));
+  const size_t esz = dtype == KNN_DTYPE_F16 ? 2 : 4;
+  if (where == 1) {
+    KNN_CUDA(knn::launch_convert_rows(rows, dtype == KNN_DTYPE_F16, n, dim, h->data, ld,
+                                      h->norms, h->stream));
+    g_dispatch.fetch_add(1);
+  } else {
+    // host rows: stage through a device buffer in chunks of <= 256 MiB
+    const int64_t chunk = std::max<int64_t>(1, (int64_t(256) << 20) / (dim * esz));
+    DevBuf stage;
+    int st = stage.ensure(static_cast<size_t>(std::min(chunk, n)) * dim * esz);
+    if (st != KNN_OK) return st;
+    for (int64_t r0 = 0; r0 < n; r0 += chunk) {
+      const int64_t rr = std::min(chunk, n - r0);
+      const char* src = static_cast<const char*>(rows) + static_cast<size_t>(r0) * dim * esz;
+      cudaError_t e = cudaMemcpyAsync(stage.ptr, src, static_cast<size_t>(rr) * dim * esz,
+                                      cudaMemcpyHostToDevice, h->stream);
+      if (e == cudaSuccess)
+        e = knn::launch_convert_rows(stage.ptr, dtype == KNN_DTYPE_F16, rr, dim,
+                                     h->data + static_cast<size_t>(r0) * ld, ld, h->norms + r0,
+                                     h->stream);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(h->stream);
+      if (e != cudaSuccess) {
+        stage.release();
+        return fail(KNN_ECUDA, "dataset upload: %s", cudaGetErrorString(e));
+      }
+      g_dispatch.fetch_add(1);
+    }
+    stage.release();
+  }
+  KNN_CUDA(cudaStreamSynchronize(h->stream));
+  int st = encode_rows(&h->xmap, h->data, n, ld, knn::kTileRows);
+  if (st != KNN_OK) return st;
+  h->n = n;
+  h->dim = dim;
+  h->ld = ld;
+  h->metric = metric;
+  h->row_offset = row_offset;
+  h->total_rows = total_rows;
+  return KNN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* knn_last_error(void) { return g_last_error.c_str(); }
+
+const char* knn_status_string(int status) {
+  switch (status) {
+    case KNN_OK: return "KNN_OK";
+    case KNN_EINVAL: return "KNN_EINVAL";
+    case KNN_ECUDA: return "KNN_ECUDA";
+    case KNN_ENCCL: return "KNN_ENCCL";
+    case KNN_ETIMEOUT: return "KNN_ETIMEOUT";
+    case KNN_ENOMEM: return "KNN_ENOMEM";
+    case KNN_EUNSUPPORTED: return "KNN_EUNSUPPORTED";
+    default: return "KNN_UNKNOWN";
+  }
+}
+
+int knn_index_create(int device, knn_index** out) {
+  if (!out) return fail(KNN_EINVAL, "null output handle");
+  *out = nullptr;
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    return fail(KNN_ECUDA, "no CUDA device available (%s)", cudaGetErrorString(e));
+  }
+  if (device < 0 || device >= count)
+    return fail(KNN_EINVAL, "device %d out of range (%d devices)", device, count);
+  cudaDeviceProp prop;
+  KNN_CUDA(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10)
+    return fail(KNN_EUNSUPPORTED, "device %d is sm_%d%d; this engine is built for sm_100a",
+                device, prop.major, prop.minor);
+  KNN_CUDA(cudaSetDevice(device));
+  knn_index* h = new knn_index();
+  h->device = device;
+  h->num_sms = prop.multiProcessorCount;
+  e = cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&h->err_dev, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(h->err_dev, 0, sizeof(int));
+  if (e == cudaSuccess) e = cudaMallocHost(&h->err_host, sizeof(int));
+  for (int i = 0; i < 4 && e == cudaSuccess; ++i) e = cudaEventCreate(&h->ev[i]);
+  if (e != cudaSuccess) {
+    knn_index_destroy(h);
+    return fail(KNN_ECUDA, "index setup: %s", cudaGetErrorString(e));
+  }
+  *h->err_host = 0;
+  h->stream = h->own_stream;
+  *out = h;
+  return KNN_OK;
+}
+
+int knn_index_destroy(knn_index* h) {
+  if (!h) return KNN_OK;
+  cudaSetDevice(h->device);
+  if (h->stream) cudaStreamSynchronize(h->stream);
+  if (h->comm) nccl().CommDestroy(h->comm);
+  for (DevBuf* b : {&h->q32, &h->q16, &h->qnorm, &h->part_d, &h->part_i, &h->out_d, &h->out_i,
+                    &h->gather_send, &h->gather_recv})
+    b->release();
+  if (h->data) cudaFree(h->data);
+  if (h->norms) cudaFree(h->norms);
+  if (h->err_dev) cudaFree(h->err_dev);
+  if (h->err_host) cudaFreeHost(h->err_host);
+  for (auto& ev : h->ev)
+    if (ev) cudaEventDestroy(ev);
+  if (h->own_stream) cudaStreamDestroy(h->own_stream);
+  delete h;
+  return KNN_OK;
+}
+
+int knn_index_set_stream(knn_index* h, void* stream) {
+  if (!h) return fail(KNN_EINVAL, "null index");
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->stream = stream ? static_cast<cudaStream_t>(stream) : h->own_stream;
+  return KNN_OK;
+}
+
+int knn_index_build(knn_index* h, const void* rows, int dtype, int64_t n, int64_t dim,
+                    int metric) {
+  return build_impl(h, rows, dtype, n, dim, metric, 0, n);
+}
+
+int knn_index_build_shard(knn_index* h, const void* rows, int dtype, int64_t n, int64_t dim,
+                          int metric, int64_t row_offset, int64_t total_rows) {
+  return build_impl(h, rows, dtype, n, dim, metric, row_offset, total_rows);
+}
+
+int64_t knn_index_rows(const knn_index* h) { return h ? h->n : 0; }
+int64_t knn_index_dim(const knn_index* h) { return h ? h->dim : 0; }
+
+int knn_index_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
+                     uint32_t* neighbors, float* distances) {
+  return search_impl(h, queries, nq, k, neighbors, distances, false, true, false);
+}
+
+int knn_index_search_i64(knn_index* h, const float* queries, int64_t nq, int64_t k,
+                         int64_t* neighbors, float* distances) {
+  return search_impl(h, queries, nq, k, neighbors, distances, true, true, false);
+}
+
+int knn_index_search_async(knn_index* h, const float* queries, int64_t nq, int64_t k,
+                           uint32_t* neighbors, float* distances) {
+  return search_impl(h, queries, nq, k, neighbors, distances, false, false, true);
+}
+
+int knn_index_sync(knn_index* h) {
+  if (!h) return fail(KNN_EINVAL, "null index");
+  std::lock_guard<std::mutex> lock(h->mu);
+  KNN_CUDA(cudaSetDevice(h->device));
+  KNN_CUDA(cudaMemcpyAsync(h->err_host, h->err_dev, sizeof(int), cudaMemcpyDeviceToHost,
+                           h->stream));
+  int st = sync_stream(h);
+  if (st != KNN_OK) return st;
+  return check_device_error(h);
+}
+
+int knn_plan_search(int64_t n_rows, int64_t dim, int64_t nq, int64_t k, int num_sms,
+                    knn_plan* out) {
+  if (!out) return fail(KNN_EINVAL, "null plan");
+  if (n_rows <= 0 || dim <= 0 || nq <= 0 || k <= 0)
+    return fail(KNN_EINVAL, "plan needs positive n_rows, dim, n_queries and k");
+  Plan p;
+  const int st = knn::plan_search(n_rows, dim, nq, k, num_sms, &p);
+  if (st != 0) return fail(st, "k = %lld is outside the engine's limits", (long long)k);
+  out->query_block = p.query_block;
+  out->query_tiles = p.query_tiles;
+  out->row_tiles = p.row_tiles;
+  out->splits = p.splits;
+  out->units = p.units;
+  out->grid = p.grid;
+  out->stages = p.stages;
+  out->smem_bytes = p.smem_bytes;
+  out->partial_bytes = p.partial_bytes;
+  return KNN_OK;
+}
+
+int knn_shard_range(int64_t n_rows, int n_ranks, int rank, int64_t* begin, int64_t* end) {
+  if (n_rows < 0 || n_ranks <= 0 || rank < 0 || rank >= n_ranks || !begin || !end)
+    return fail(KNN_EINVAL, "invalid shard request");
+  const int64_t per = (n_rows + n_ranks - 1) / n_ranks;
+  int64_t b = per * rank;
+  int64_t e = b + per;
+  if (b > n_rows) b = n_rows;
+  if (e > n_rows) e = n_rows;
+  *begin = b;
+  *end = e;
+  return KNN_OK;
+}
+
+int knn_comm_unique_id(void* out) {
+  if (!out) return fail(KNN_EINVAL, "null output");
+  static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+  ncclUniqueId id;
+  if (!nccl().ok) return fail(KNN_ENCCL, "NCCL unavailable: %s", nccl().why.c_str());
+  ncclResult_t r = nccl().GetUniqueId(&id);
+  if (r != ncclSuccess) return fail(KNN_ENCCL, "ncclGetUniqueId: %s", nccl_str(r));
+  std::memcpy(out, &id, sizeof(id));
+  return KNN_OK;
+}
+
+int knn_index_attach_comm(knn_index* h, const void* uid, int n_ranks, int rank) {
+  if (!h || !uid || n_ranks <= 0 || rank < 0 || rank >= n_ranks)
+    return fail(KNN_EINVAL, "invalid communicator request");
+  std::lock_guard<std::mutex> lock(h->mu);
+  KNN_CUDA(cudaSetDevice(h->device));
+  if (h->comm) {
+    nccl().CommDestroy(h->comm);
+    h->comm = nullptr;
+  }
+  if (n_ranks == 1) {
+    h->n_ranks = 1;
+    h->rank = 0;
+    return KNN_OK;
+  }
+  ncclUniqueId id;
+  std::memcpy(&id, uid, sizeof(id));
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  if (!nccl().ok) return fail(KNN_ENCCL, "NCCL unavailable: %s", nccl().why.c_str());
+  ncclResult_t r = nccl().CommInitRankConfig(&h->comm, n_ranks, id, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    h->comm = nullptr;
+    return fail(KNN_ENCCL, "ncclCommInitRankConfig: %s", nccl_str(r));
+  }
+  int st = poll_nccl(h, 120.0);
+  if (st != KNN_OK) return st;
+  h->n_ranks = n_ranks;
+  h->rank = rank;
+  return KNN_OK;
+}
+
+int knn_index_set_profiling(knn_index* h, int enabled) {
+  if (!h) return fail(KNN_EINVAL, "null index");
+  h->profiling = enabled != 0;
+  return KNN_OK;
+}
+
+int knn_index_kernel_stats(knn_index* h, double* scan_ms, double* merge_ms,
+                           int64_t* scan_launches, int64_t* kernel_launches) {
+  if (!h) return fail(KNN_EINVAL, "null index");
+  if (scan_ms) *scan_ms = h->scan_ms;
+  if (merge_ms) *merge_ms = h->merge_ms;
+  if (scan_launches) *scan_launches = h->scan_launches;
+  if (kernel_launches) *kernel_launches = h->kernel_launches;
+  return KNN_OK;
+}
+
+int knn_index_reset_kernel_stats(knn_index* h) {
+  if (!h) return fail(KNN_EINVAL, "null index");
+  h->scan_ms = h->merge_ms = 0.0;
+  h->scan_launches = h->kernel_launches = 0;
+  return KNN_OK;
+}
+
+int knn_selftest_bounded_wait(int device, int64_t limit_us) {
+  if (limit_us <= 0 || limit_us > 2000000) return fail(KNN_EINVAL, "limit_us out of range");
+  KNN_CUDA(cudaSetDevice(device));
+  int* err = nullptr;
+  KNN_CUDA(cudaMalloc(&err, sizeof(int)));
+  int host = 0;
+  cudaError_t e = cudaMemset(err, 0, sizeof(int));
+  if (e == cudaSuccess)
+    e = knn::launch_bounded_wait_selftest(err, static_cast<uint64_t>(limit_us) * 1000u, nullptr);
+  if (e == cudaSuccess) e = cudaMemcpy(&host, err, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaFree(err);
+  if (e != cudaSuccess) return fail(KNN_ECUDA, "self-test: %s", cudaGetErrorString(e));
+  g_dispatch.fetch_add(1);
+  if (host != 0)
+    return fail(KNN_ETIMEOUT, "bounded wait gave up as designed (device code %d)", host);
+  return fail(KNN_ECUDA, "bounded wait returned without timing out");
+}
+
+uint64_t knn_dispatch_count(void) { return g_dispatch.load(); }
+void knn_reset_dispatch_count(void) { g_dispatch.store(0); }
+
+}  // extern "C"

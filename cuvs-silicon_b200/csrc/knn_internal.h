@@ -1,0 +1,78 @@
+// knn_internal.h -- declarations shared by the engine's translation units.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace knn {
+
+// Scan-kernel geometry (fixed for sm_100a).
+constexpr int kTileRows = 256;    // dataset rows per tile = UMMA N
+constexpr int kQueryRows = 128;   // query rows per tile  = UMMA M
+constexpr int kKChunk = 64;       // fp16 per 128-byte swizzled row segment
+constexpr int kStageA = kQueryRows * kKChunk * 2;  // 16 KiB query slab
+constexpr int kStageB = kTileRows * kKChunk * 2;   // 32 KiB dataset slab
+constexpr int kStageBytes = kStageA + kStageB;     // 48 KiB per stage
+constexpr int kAccCols = 256;     // TMEM columns per accumulator
+constexpr int kTmemCols = 512;    // double-buffered accumulators
+constexpr int kScanThreads = 192; // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kMaxStages = 8;
+constexpr int kSmemLimit = 232448;        // sm_100 opt-in dynamic smem per CTA
+constexpr int kSmemReserve = 1024 + 256;  // 1 KiB alignment slack + barriers
+constexpr int kMaxK = 512;
+constexpr uint32_t kNoIndex = 0xFFFFFFFFu;
+
+struct ScanParams {
+  const float* row_norms;    // [n_rows]
+  const float* query_norms;  // [n_queries]
+  float* part_d;             // [n_queries][splits][k]
+  uint32_t* part_i;          // [n_queries][splits][k]
+  int* err;                  // device error word (0 = ok)
+  int64_t n_rows;
+  int64_t n_queries;
+  int64_t row_tiles;
+  int32_t k;
+  int32_t query_block;  // query rows owned per work unit (multiple of 32, <= 128)
+  int32_t query_tiles;
+  int32_t splits;
+  int32_t units;
+  int32_t k_chunks;  // ceil(ld / 64)
+  int32_t stages;
+  int32_t dataset_evict_first;
+};
+
+struct Plan {
+  int64_t query_block, query_tiles, row_tiles, splits, units, grid, stages;
+  int64_t smem_bytes, partial_bytes;
+};
+
+// Returns 0 and fills `out`, or a KNN_E* status (KNN_EUNSUPPORTED when k is
+// too large for the shared-memory budget).
+int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int num_sms,
+                Plan* out);
+
+// Launchers (return the CUDA error of the launch).
+cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
+                        const ScanParams& p, const Plan& plan, cudaStream_t stream);
+
+// fp32/fp16 rows -> fp16 rows with leading dimension ld (zero padded) plus
+// fp32 norms of the rounded rows.  in_is_half selects the input type.
+cudaError_t launch_convert_rows(const void* in, bool in_is_half, int64_t rows,
+                                int64_t dim, __half* out, int64_t ld, float* norms,
+                                cudaStream_t stream);
+
+// Launches the bounded-wait self-test kernel (see knn_scan.cu).
+cudaError_t launch_bounded_wait_selftest(int* err, uint64_t limit_ns, cudaStream_t stream);
+
+// Merges n_lists sorted top-k lists per query into the final top-k.
+// List l of query q starts at in_{d,i}[q * stride_query + l * stride_list].
+// Valid indices get index_offset added.  out_i is uint32 (no-neighbour =
+// UINT32_MAX) or int64 (no-neighbour = -1) per out_i64.
+cudaError_t launch_merge(const float* in_d, const uint32_t* in_i, int64_t stride_list,
+                         int64_t stride_query, int n_lists, int k, int64_t n_queries,
+                         int64_t index_offset, float* out_d, void* out_i, bool out_i64,
+                         cudaStream_t stream);
+
+}  // namespace knn

@@ -1,0 +1,122 @@
+// knn_prep.cu -- row conversion + norms, used at build time for the dataset
+// and per search for the queries.
+//
+// Replaces the reference's host loops that cast the dataset and queries to
+// fp16 (src/metal_context.mm:164-166,195-196) and compute fp32 row norms
+// (compute_row_norms, src/metal_context.mm:127-137).  Two deliberate
+// differences: the work runs on the GPU (one warp per row, coalesced,
+// 16-byte vector loads/stores when the row layout allows), and the norm is
+// taken over the fp16-ROUNDED values, so |q|^2 + |x|^2 - 2 q.x is the exact
+// expansion of the squared distance between the stored vectors.
+//
+// Output rows have leading dimension ld >= dim (a multiple of 8 halves, so
+// every row starts on a 16-byte boundary as TMA requires); the pad columns
+// are written as zeros and contribute nothing to dot products or norms.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "knn_internal.h"
+
+namespace knn {
+
+namespace {
+
+template <bool kHalfIn>
+__device__ __forceinline__ float load_elem(const void* in, int64_t i) {
+  if constexpr (kHalfIn) {
+    return __half2float(static_cast<const __half*>(in)[i]);
+  } else {
+    return static_cast<const float*>(in)[i];
+  }
+}
+
+// One warp per row, grid-stride over rows.  `vec` selects the 8-wide path:
+// dim % 8 == 0 and the input base 16-byte aligned.
+template <bool kHalfIn>
+__global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, int64_t dim,
+                                    __half* __restrict__ out, int64_t ld,
+                                    float* __restrict__ norms, bool vec) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps_per_block = blockDim.x >> 5;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * warps_per_block + (threadIdx.x >> 5);
+  const int64_t step = static_cast<int64_t>(gridDim.x) * warps_per_block;
+  for (int64_t r = first; r < rows; r += step) {
+    float acc = 0.0f;
+    __half* orow = out + r * ld;
+    if (vec) {
+      const int64_t groups = dim / 8;
+      for (int64_t g = lane; g < groups; g += 32) {
+        float v[8];
+        if constexpr (kHalfIn) {
+          const uint4 raw = reinterpret_cast<const uint4*>(static_cast<const __half*>(in) +
+                                                           r * dim)[g];
+          const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(h[j]);
+            v[2 * j] = f.x;
+            v[2 * j + 1] = f.y;
+          }
+        } else {
+          const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(in) +
+                                                              r * dim) + 2 * g;
+          const float4 a = src[0];
+          const float4 b = src[1];
+          v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+          v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        }
+        uint4 packed;
+        __half2* h2 = reinterpret_cast<__half2*>(&packed);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+          h2[j] = h;
+          const float2 f = __half22float2(h);
+          acc = fmaf(f.x, f.x, acc);
+          acc = fmaf(f.y, f.y, acc);
+        }
+        reinterpret_cast<uint4*>(orow)[g] = packed;
+      }
+      // zero padding [dim, ld): dim is a multiple of 8 here
+      for (int64_t c = dim + lane; c < ld; c += 32) orow[c] = __float2half_rn(0.0f);
+    } else {
+      for (int64_t c = lane; c < ld; c += 32) {
+        __half h = __float2half_rn(0.0f);
+        if (c < dim) {
+          h = __float2half_rn(load_elem<kHalfIn>(in, r * dim + c));
+          const float f = __half2float(h);
+          acc = fmaf(f, f, acc);
+        }
+        orow[c] = h;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) norms[r] = acc;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_convert_rows(const void* in, bool in_is_half, int64_t rows, int64_t dim,
+                                __half* out, int64_t ld, float* norms, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  const bool vec = (dim % 8 == 0) && ((reinterpret_cast<uintptr_t>(in) & 15u) == 0) &&
+                   ((reinterpret_cast<uintptr_t>(out) & 15u) == 0) && (ld % 8 == 0);
+  constexpr int kThreads = 256;
+  const int64_t warps_needed = rows;
+  int64_t blocks = (warps_needed + (kThreads / 32) - 1) / (kThreads / 32);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (in_is_half) {
+    convert_rows_kernel<true><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
+        in, rows, dim, out, ld, norms, vec);
+  } else {
+    convert_rows_kernel<false><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
+        in, rows, dim, out, ld, norms, vec);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace knn

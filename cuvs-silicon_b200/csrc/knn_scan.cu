@@ -1,0 +1,440 @@
+// knn_scan.cu -- the fused exact-L2 scan kernel for sm_100a.
+//
+// Replaces the reference's two passes, MPS fp16 GEMM into a Q x N fp32
+// `cross` buffer (src/metal_context.mm:202-225) followed by the
+// l2_topk_from_cross kernel (shaders/cagra_kernels.metal:604-653), with one
+// kernel in which the Q x N matrix never leaves the SM:
+//
+//   warp 0  (1 thread)  TMA producer: per 64-wide slice of the dimension, a
+//                       128-row query slab and a 256-row dataset slab, both
+//                       128-byte swizzled, into a ring of shared-memory stages.
+//   warp 1  (1 thread)  tcgen05.mma issuer: 128 x 256 x 16 fp16 MMAs into an
+//                       fp32 accumulator in tensor memory (TMEM); two
+//                       accumulators of 256 columns alternate so the
+//                       epilogue of one tile overlaps the MMAs of the next.
+//   warps 2-5           epilogue: thread t owns query row t of the tile
+//                       (TMEM lane t).  tcgen05.ld brings 32 dataset columns
+//                       at a time into registers; d = |q|^2 + |x|^2 - 2 q.x
+//                       (squared L2, the expanded form of
+//                       shaders/cagra_kernels.metal:624, clamped at 0); a
+//                       per-thread threshold (the current k-th best) rejects
+//                       almost every candidate with one compare; survivors
+//                       replace the root of the thread's max-heap held in
+//                       shared memory.
+//
+// Work is split into units (query tile m, contiguous range s of dataset
+// tiles).  A persistent CTA walks units blockIdx.x, +gridDim.x, ...; at the
+// end of a unit each query's heap is sorted and written as list s of that
+// query: part[(q * splits + s) * k + r].  The merge kernel (knn_merge.cu)
+// reduces the lists to the final top-k, ordered by (distance, index) like
+// src/cagra.cpp:229-238.
+//
+// No TMA multicast is used anywhere (the same code runs under multi-GPU
+// sharding).  Every mbarrier wait is bounded (ptx.cuh).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "knn_internal.h"
+#include "ptx.cuh"
+
+namespace knn {
+
+namespace {
+
+__device__ __forceinline__ bool worse(float da, uint32_t ia, float db, uint32_t ib) {
+  return da > db || (da == db && ia > ib);
+}
+
+// Max-heap of (distance, index) stored column-wise: entry `pos` of query row
+// `row` lives at [pos * stride + row], so the 32 threads of a warp always hit
+// 32 distinct banks whatever positions they touch.
+__device__ __forceinline__ void heap_sift_down(float* hd, uint32_t* hi, int size, int stride,
+                                               int row, int pos, float d, uint32_t i) {
+  while (true) {
+    int c = 2 * pos + 1;
+    if (c >= size) break;
+    float cd = hd[c * stride + row];
+    uint32_t ci = hi[c * stride + row];
+    if (c + 1 < size) {
+      const float rd = hd[(c + 1) * stride + row];
+      const uint32_t ri = hi[(c + 1) * stride + row];
+      if (worse(rd, ri, cd, ci)) {
+        c += 1;
+        cd = rd;
+        ci = ri;
+      }
+    }
+    if (!worse(cd, ci, d, i)) break;
+    hd[pos * stride + row] = cd;
+    hi[pos * stride + row] = ci;
+    pos = c;
+  }
+  hd[pos * stride + row] = d;
+  hi[pos * stride + row] = i;
+}
+
+struct Smem {
+  uint8_t* stages;
+  float* heap_d;
+  uint32_t* heap_i;
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* acc_full;
+  uint64_t* acc_empty;
+  uint64_t* drain;
+  uint32_t* tmem_slot;
+};
+
+__device__ __forceinline__ Smem carve(uint8_t* raw, const ScanParams& p) {
+  Smem s;
+  const uint32_t base = smem_addr(raw);
+  const uint32_t pad = (1024u - (base & 1023u)) & 1023u;
+  s.stages = raw + pad;
+  s.heap_d = reinterpret_cast<float*>(s.stages + static_cast<size_t>(p.stages) * kStageBytes);
+  s.heap_i = reinterpret_cast<uint32_t*>(s.heap_d + static_cast<size_t>(p.k) * p.query_block);
+  uintptr_t b = reinterpret_cast<uintptr_t>(s.heap_i + static_cast<size_t>(p.k) * p.query_block);
+  b = (b + 7) & ~static_cast<uintptr_t>(7);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(b);
+  s.full = bars;
+  s.empty = bars + p.stages;
+  s.acc_full = bars + 2 * p.stages;
+  s.acc_empty = s.acc_full + 2;
+  s.drain = s.acc_empty + 2;
+  s.tmem_slot = reinterpret_cast<uint32_t*>(s.drain + 1);
+  return s;
+}
+
+__device__ __forceinline__ void unit_range(const ScanParams& p, int u, int& m, int64_t& t0,
+                                           int64_t& t1) {
+  m = u % p.query_tiles;
+  const int s = u / p.query_tiles;
+  t0 = static_cast<int64_t>(s) * p.row_tiles / p.splits;
+  t1 = static_cast<int64_t>(s + 1) * p.row_tiles / p.splits;
+}
+
+// Bounded wait used while unwinding after an error: ignores the error word,
+// gives up after ~10 ms.
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > 10000000ull) break;
+  }
+}
+
+__device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap, const ScanParams& p,
+                         const Smem& sm) {
+  const uint64_t pol_q = policy_evict_last();
+  const uint64_t pol_x = p.dataset_evict_first ? policy_evict_first() : policy_evict_normal();
+  uint32_t it = 0;
+  bool failed = false;
+  for (int u = blockIdx.x; u < p.units && !failed; u += gridDim.x) {
+    int m;
+    int64_t t0, t1;
+    unit_range(p, u, m, t0, t1);
+    const int32_t qy = m * p.query_block;
+    for (int64_t t = t0; t < t1 && !failed; ++t) {
+      const int32_t xy = static_cast<int32_t>(t * kTileRows);
+      for (int kc = 0; kc < p.k_chunks; ++kc) {
+        const uint32_t slot = it % p.stages;
+        const uint32_t ph = (it / p.stages) & 1u;
+        if (!mbar_wait(&sm.empty[slot], ph ^ 1u, p.err, kErrTimeoutEmpty)) {
+          failed = true;
+          break;
+        }
+        uint8_t* st = sm.stages + static_cast<size_t>(slot) * kStageBytes;
+        mbar_arrive_expect_tx(&sm.full[slot], kStageBytes);
+        tma_load_2d(st, qmap, &sm.full[slot], kc * kKChunk, qy, pol_q);
+        tma_load_2d(st + kStageA, xmap, &sm.full[slot], kc * kKChunk, xy, pol_x);
+        ++it;
+      }
+    }
+  }
+  if (failed) {
+    // Let the copies already issued land before the CTA can retire.
+    const uint32_t outstanding = it < static_cast<uint32_t>(p.stages) ? it : p.stages;
+    for (uint32_t j = it - outstanding; j < it; ++j)
+      drain_wait(&sm.full[j % p.stages], (j / p.stages) & 1u);
+  }
+}
+
+__device__ void mma_issuer(const ScanParams& p, const Smem& sm, uint32_t tmem_base) {
+  constexpr uint32_t idesc = idesc_f16_f32(kQueryRows, kTileRows);
+  uint32_t it = 0, tc = 0;
+  bool failed = false;
+  for (int u = blockIdx.x; u < p.units && !failed; u += gridDim.x) {
+    int m;
+    int64_t t0, t1;
+    unit_range(p, u, m, t0, t1);
+    for (int64_t t = t0; t < t1 && !failed; ++t) {
+      const uint32_t b = tc & 1u;
+      if (!mbar_wait(&sm.acc_empty[b], ((tc >> 1) & 1u) ^ 1u, p.err, kErrTimeoutAccEmpty)) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + b * kAccCols;
+      for (int kc = 0; kc < p.k_chunks; ++kc) {
+        const uint32_t slot = it % p.stages;
+        if (!mbar_wait(&sm.full[slot], (it / p.stages) & 1u, p.err, kErrTimeoutFull)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_addr(sm.stages + static_cast<size_t>(slot) * kStageBytes);
+        const uint32_t b0 = a0 + kStageA;
+#pragma unroll
+        for (int kk = 0; kk < kKChunk / 16; ++kk) {
+          // advancing 16 fp16 (32 bytes) inside the 128-byte swizzle atom
+          umma_f16_ss(d_tmem, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32),
+                      idesc, (kc | kk) != 0 ? 1u : 0u);
+        }
+        umma_commit(&sm.empty[slot]);
+        ++it;
+      }
+      if (failed) break;
+      umma_commit(&sm.acc_full[b]);
+      ++tc;
+    }
+  }
+  // All MMAs of this thread must be complete before TMEM is released.
+  umma_commit(sm.drain);
+  drain_wait(sm.drain, 0);
+}
+
+__device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base, int warp,
+                         int lane) {
+  const int quad = warp & 3;              // TMEM lane quadrant this warp may access
+  const int row = quad * 32 + lane;       // query row within the unit's block
+  const bool warp_active = quad * 32 < p.query_block;
+  const int stride = p.query_block;
+  const int k = p.k;
+  uint32_t tc = 0;
+  bool failed = false;
+  for (int u = blockIdx.x; u < p.units && !failed; u += gridDim.x) {
+    int m;
+    int64_t t0, t1;
+    unit_range(p, u, m, t0, t1);
+    const int64_t q = static_cast<int64_t>(m) * p.query_block + row;
+    const bool valid_q = warp_active && row < p.query_block && q < p.n_queries;
+    const float qn = valid_q ? p.query_norms[q] : 0.0f;
+    if (valid_q) {
+      for (int pos = 0; pos < k; ++pos) {
+        sm.heap_d[pos * stride + row] = __int_as_float(0x7f800000);
+        sm.heap_i[pos * stride + row] = kNoIndex;
+      }
+    }
+    float thr = valid_q ? __int_as_float(0x7f800000) : __int_as_float(0xff800000);
+    for (int64_t t = t0; t < t1; ++t) {
+      const uint32_t b = tc & 1u;
+      // every lane waits; the warp leaves together if any lane gave up, so
+      // the .sync.aligned TMEM loads below always see a converged warp
+      const bool ok = mbar_wait(&sm.acc_full[b], (tc >> 1) & 1u, p.err, kErrTimeoutAccFull);
+      if (__any_sync(0xffffffffu, !ok)) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      if (warp_active) {
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + b * kAccCols;
+#pragma unroll 1
+        for (int c = 0; c < kAccCols / 32; ++c) {
+          // row norm of column (c * 32 + lane); its load overlaps the TMEM load
+          const int64_t col = t * kTileRows + c * 32 + lane;
+          const float xn = col < p.n_rows ? __ldg(p.row_norms + col) : __int_as_float(0x7f800000);
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, r);
+          tmem_ld_wait();
+          float dv[32];
+          uint32_t mask = 0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float xj = __shfl_sync(0xffffffffu, xn, j);
+            float d = fmaf(-2.0f, __uint_as_float(r[j]), qn + xj);
+            d = d < 0.0f ? 0.0f : d;
+            dv[j] = d;
+            mask |= (d < thr ? 1u : 0u) << j;
+          }
+          if (mask) {
+            const uint32_t col0 = static_cast<uint32_t>(t * kTileRows + c * 32);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (((mask >> j) & 1u) && dv[j] < thr) {
+                heap_sift_down(sm.heap_d, sm.heap_i, k, stride, row, 0, dv[j], col0 + j);
+                thr = sm.heap_d[row];
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
+      ++tc;
+    }
+    if (failed) break;
+    if (valid_q) {
+      // heap sort -> ascending (distance, index)
+      for (int end = k - 1; end > 0; --end) {
+        const float rd = sm.heap_d[row];
+        const uint32_t ri = sm.heap_i[row];
+        const float ed = sm.heap_d[end * stride + row];
+        const uint32_t ei = sm.heap_i[end * stride + row];
+        sm.heap_d[end * stride + row] = rd;
+        sm.heap_i[end * stride + row] = ri;
+        heap_sift_down(sm.heap_d, sm.heap_i, end, stride, row, 0, ed, ei);
+      }
+      const int s = u / p.query_tiles;
+      float* od = p.part_d + (static_cast<size_t>(q) * p.splits + s) * k;
+      uint32_t* oi = p.part_i + (static_cast<size_t>(q) * p.splits + s) * k;
+      for (int r = 0; r < k; ++r) {
+        od[r] = sm.heap_d[r * stride + row];
+        oi[r] = sm.heap_i[r * stride + row];
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kScanThreads, 1)
+    knn_scan_kernel(const __grid_constant__ CUtensorMap qmap,
+                    const __grid_constant__ CUtensorMap xmap, const ScanParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const Smem sm = carve(smem_raw, p);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.acc_full[b], 1);
+      mbar_init(&sm.acc_empty[b], 4);
+    }
+    mbar_init(sm.drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&qmap);
+    tma_prefetch_map(&xmap);
+  }
+  if (warp == 1) {
+    tmem_alloc(sm.tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *sm.tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) producer(&qmap, &xmap, p, sm);
+  } else if (warp == 1) {
+    if (lane == 0) mma_issuer(p, sm, tmem_base);
+  } else {
+    epilogue(p, sm, tmem_base, warp, lane);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// Self-test of the bounded wait: thread 0 waits for phase 0 of a barrier
+// that nothing arrives on; the wait must give up after limit_ns and record
+// kErrTimeoutFull.  No memory access depends on the barrier.
+__global__ void bounded_wait_selftest_kernel(int* err, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, err, kErrTimeoutFull, limit_ns);
+}
+
+}  // namespace
+
+cudaError_t launch_bounded_wait_selftest(int* err, uint64_t limit_ns, cudaStream_t stream) {
+  bounded_wait_selftest_kernel<<<1, 32, 0, stream>>>(err, limit_ns);
+  return cudaGetLastError();
+}
+
+int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int num_sms,
+                Plan* out) {
+  if (n_rows <= 0 || dim <= 0 || n_queries <= 0 || k <= 0 || !out) return 1;
+  if (k > kMaxK) return 6;
+  if (num_sms <= 0) num_sms = 148;
+  const int64_t heap_per_query = k * 8;
+  const int64_t budget = kSmemLimit - kSmemReserve;
+  int64_t qb_cap = (budget - 2 * kStageBytes) / heap_per_query;
+  qb_cap = (qb_cap / 32) * 32;
+  if (qb_cap > kQueryRows) qb_cap = kQueryRows;
+  if (qb_cap < 32) return 6;
+  int64_t qb = ((n_queries + 31) / 32) * 32;
+  if (qb > qb_cap) qb = qb_cap;
+  int64_t stages = (budget - qb * heap_per_query) / kStageBytes;
+  if (stages > kMaxStages) stages = kMaxStages;
+  if (stages < 2) return 6;
+  const int64_t query_tiles = (n_queries + qb - 1) / qb;
+  const int64_t row_tiles = (n_rows + kTileRows - 1) / kTileRows;
+  int64_t splits;
+  if (query_tiles == 1) {
+    splits = row_tiles < num_sms ? row_tiles : num_sms;
+  } else {
+    // Pick the split count minimising waves x (tiles per unit + 1), with the
+    // partial lists capped at 1 GiB.
+    const int64_t max_s = row_tiles < 4 * num_sms ? row_tiles : 4 * num_sms;
+    splits = 1;
+    double best = -1.0;
+    for (int64_t s = 1; s <= max_s; ++s) {
+      if (n_queries * s * k * 8 > (int64_t(1) << 30) && s > 1) break;
+      const int64_t units = query_tiles * s;
+      const int64_t waves = (units + num_sms - 1) / num_sms;
+      const int64_t per_unit = (row_tiles + s - 1) / s;
+      const double cost = static_cast<double>(waves) * static_cast<double>(per_unit + 1);
+      if (best < 0 || cost < best) {
+        best = cost;
+        splits = s;
+      }
+    }
+  }
+  const int64_t units = query_tiles * splits;
+  if (units > INT32_MAX || row_tiles * kTileRows > INT32_MAX + int64_t(kTileRows)) return 6;
+  out->query_block = qb;
+  out->query_tiles = query_tiles;
+  out->row_tiles = row_tiles;
+  out->splits = splits;
+  out->units = units;
+  out->grid = units < num_sms ? units : num_sms;
+  out->stages = stages;
+  out->smem_bytes = kSmemReserve + stages * kStageBytes + qb * heap_per_query;
+  out->partial_bytes = n_queries * splits * k * 8;
+  (void)dim;
+  return 0;
+}
+
+cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap, const ScanParams& p,
+                        const Plan& plan, cudaStream_t stream) {
+  // the opt-in shared-memory limit is a per-device function attribute
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    e = cudaFuncSetAttribute(knn_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemLimit));
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  knn_scan_kernel<<<static_cast<unsigned>(plan.grid), kScanThreads,
+                    static_cast<size_t>(plan.smem_bytes), stream>>>(qmap, xmap, p);
+  return cudaGetLastError();
+}
+
+}  // namespace knn

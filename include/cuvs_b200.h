@@ -1,0 +1,198 @@
+/*
+ * cuvs_b200.h -- C ABI of the B200 exact brute-force k-NN engine.
+ *
+ * This is the drop-in boundary for the reference's exact L2 search path
+ * (ysys143/cuvs-silicon): everything the reference's C++ layer asks of its
+ * device runtime for that path is one of the functions below.  Plain C
+ * types only: pointers, sizes and int status codes.  Pointers may be host
+ * or device memory; the engine classifies them and stages host buffers.
+ *
+ * Reference interfaces replaced (file:line in the reference repository):
+ *   knn_index_create / knn_index_destroy
+ *       cuvs_silicon::MetalContext::instance() / is_available()
+ *       (include/cuvs_silicon/metal_context.hpp:15-19,
+ *        src/metal_context.mm:59-101)
+ *   knn_index_build
+ *       the lazy dataset cache of search_brute_force: fp16 copy of the
+ *       dataset and fp32 row norms keyed on (ptr, N, D)
+ *       (src/metal_context.mm:22-55,155-175), moved to build time, plus the
+ *       validation of cuvs::neighbors::cagra::build (src/cagra.cpp:26-32)
+ *   knn_index_search
+ *       MetalContext::search_brute_force (metal_context.hpp:36-41,
+ *       src/metal_context.mm:139-255), reached from cagra::search
+ *       (src/cagra.cpp:197-202) and, on hosts without a GPU, its CPU exact
+ *       path (src/cagra.cpp:211-252) whose output contract it keeps:
+ *       squared L2, ascending (distance, index), k > n padded with
+ *       UINT32_MAX / +inf
+ *   knn_dispatch_count / knn_reset_dispatch_count
+ *       cuvs::neighbors::cagra::metal_dispatch_count /
+ *       reset_metal_dispatch_count (include/cuvs/neighbors/cagra.hpp:119-122,
+ *       src/cagra.cpp:258-266,369-371)
+ *
+ * Functions with no counterpart in the reference (it runs on one device and
+ * has no configuration surface) say so in their comment.
+ *
+ * Status codes: every function returning int returns KNN_OK (0) or one of
+ * the KNN_E* codes; knn_last_error() then describes the failure (thread
+ * local).  The C++ layer maps KNN_EINVAL to std::invalid_argument and the
+ * rest to std::runtime_error, as the reference throws
+ * (src/cagra.cpp:26-32,100-111; src/metal_context.mm:146-147,245-246).
+ */
+#ifndef CUVS_B200_H_
+#define CUVS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KNN_OK 0
+#define KNN_EINVAL 1       /* invalid argument (reference: invalid_argument) */
+#define KNN_ECUDA 2        /* CUDA runtime/driver error or no usable GPU */
+#define KNN_ENCCL 3        /* NCCL error */
+#define KNN_ETIMEOUT 4     /* a bounded device wait expired */
+#define KNN_ENOMEM 5       /* device or host allocation failed */
+#define KNN_EUNSUPPORTED 6 /* valid request outside the engine's limits */
+
+#define KNN_DTYPE_F32 0
+#define KNN_DTYPE_F16 1
+
+#define KNN_METRIC_L2_EXPANDED 0 /* cuvs::distance::DistanceType::L2Expanded */
+#define KNN_METRIC_INNER_PRODUCT 1
+
+/* Largest k one search accepts (per-CTA top-k state must fit in shared
+ * memory next to a two-stage pipeline).  The reference's Metal kernel caps k
+ * at 16 (shaders/cagra_kernels.metal:538); its CPU path has no cap. */
+#define KNN_MAX_K 512
+
+/* UINT32_MAX marks "no neighbour" (src/cagra.cpp:248-249). */
+#define KNN_NO_INDEX 0xFFFFFFFFu
+
+typedef struct knn_index knn_index;
+
+/* Search-plan description (host-side planner; no counterpart in the
+ * reference, exposed for tests and tooling). */
+typedef struct knn_plan {
+  int64_t query_block;   /* queries per CTA work unit (multiple of 32) */
+  int64_t query_tiles;   /* ceil(n_queries / query_block) */
+  int64_t row_tiles;     /* ceil(n_rows / 256) */
+  int64_t splits;        /* row-range splits per query tile */
+  int64_t units;         /* query_tiles * splits */
+  int64_t grid;          /* persistent CTAs launched */
+  int64_t stages;        /* shared-memory pipeline stages */
+  int64_t smem_bytes;    /* dynamic shared memory per CTA */
+  int64_t partial_bytes; /* scratch for per-unit top-k lists */
+} knn_plan;
+
+/* Human-readable text for the calling thread's last failure. */
+const char* knn_last_error(void);
+/* Static name of a status code. */
+const char* knn_status_string(int status);
+
+/* Creates an empty index bound to CUDA device `device`.  Replaces the
+ * reference's MetalContext singleton (metal_context.hpp:15-19); one index
+ * per dataset instead of one process-wide cache keyed on a raw pointer. */
+int knn_index_create(int device, knn_index** out);
+int knn_index_destroy(knn_index* index);
+
+/* Orders the index's work on a caller-owned cudaStream_t (NULL restores the
+ * index's own stream).  No counterpart: the reference blocks on every
+ * command buffer (src/metal_context.mm:222-225,242-243). */
+int knn_index_set_stream(knn_index* index, void* cuda_stream);
+
+/* Loads `rows` (n_rows x dim, row-major, fp32 or fp16, host or device) into
+ * device HBM as fp16 rows (round-to-nearest-even) and fills the fp32 row
+ * norms ||x16||^2.  Replaces the first-search cache fill of
+ * search_brute_force (src/metal_context.mm:155-175) and the checks of
+ * cagra::build (src/cagra.cpp:26-32): only L2 (and inner product) metrics,
+ * non-null non-empty data.  n_rows must be below 2^32 - 1 (neighbour indices
+ * are uint32, cagra.hpp:54-55). */
+int knn_index_build(knn_index* index, const void* rows, int dtype,
+                    int64_t n_rows, int64_t dim, int metric);
+
+/* Same as knn_index_build for one row shard of a larger dataset: rows
+ * [row_offset, row_offset + n_rows) of a total_rows-row dataset.  Neighbour
+ * indices reported by searches are global (row_offset added).  No
+ * counterpart: the reference runs on one device. */
+int knn_index_build_shard(knn_index* index, const void* rows, int dtype,
+                          int64_t n_rows, int64_t dim, int metric,
+                          int64_t row_offset, int64_t total_rows);
+
+int64_t knn_index_rows(const knn_index* index);
+int64_t knn_index_dim(const knn_index* index);
+
+/* Exact k-NN of n_queries fp32 queries (host or device, row-major, index
+ * dim columns).  Writes neighbours (uint32) and squared distances (fp32),
+ * each n_queries x k, ascending by (distance, index); slots beyond the
+ * number of rows hold KNN_NO_INDEX / +inf.  Blocks until the results are in
+ * place, like the reference (src/metal_context.mm:222-252).  k == 0 or
+ * n_queries == 0 is a no-op.  When a communicator is attached
+ * (knn_index_attach_comm) every rank must call this with the same queries
+ * and k; each rank receives the merged global result.
+ * Replaces MetalContext::search_brute_force (src/metal_context.mm:139-255). */
+int knn_index_search(knn_index* index, const float* queries, int64_t n_queries,
+                     int64_t k, uint32_t* neighbors, float* distances);
+
+/* As knn_index_search with int64 neighbours (cuVS brute_force convention);
+ * "no neighbour" is written as -1.  No counterpart in the reference. */
+int knn_index_search_i64(knn_index* index, const float* queries,
+                         int64_t n_queries, int64_t k, int64_t* neighbors,
+                         float* distances);
+
+/* Stream-ordered search: all four pointers must be device memory; returns
+ * after enqueueing on the index's stream without synchronising.  Errors
+ * raised by the kernels themselves (bounded-wait timeouts) are reported by
+ * the next knn_index_sync.  No counterpart in the reference. */
+int knn_index_search_async(knn_index* index, const float* queries,
+                           int64_t n_queries, int64_t k, uint32_t* neighbors,
+                           float* distances);
+/* Waits for the index's stream and reports device-side errors. */
+int knn_index_sync(knn_index* index);
+
+/* Plans a search without running it (pure host arithmetic).  num_sms <= 0
+ * uses 148 (B200).  No counterpart in the reference. */
+int knn_plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k,
+                    int num_sms, knn_plan* out);
+
+/* Contiguous row shard [begin, end) of rank `rank` among n_ranks:
+ * begin = rank * ceil(n_rows / n_ranks), clipped to n_rows.  Pure host
+ * arithmetic.  No counterpart in the reference. */
+int knn_shard_range(int64_t n_rows, int n_ranks, int rank, int64_t* begin,
+                    int64_t* end);
+
+/* Multi-GPU, one process per GPU.  knn_comm_unique_id fills 128 bytes on one
+ * rank; the caller broadcasts them; every rank then calls
+ * knn_index_attach_comm with the same bytes.  Searches on an index with a
+ * communicator all-gather the per-rank top-k lists over NCCL and merge them
+ * on the device.  No counterpart in the reference (single device). */
+int knn_comm_unique_id(void* out_128_bytes);
+int knn_index_attach_comm(knn_index* index, const void* unique_id_128_bytes,
+                          int n_ranks, int rank);
+
+/* Kernel timing: when enabled, the engine records CUDA events around its
+ * fused scan kernel and its merge kernels on the stream they are launched on
+ * and accumulates their durations.  No counterpart in the reference. */
+int knn_index_set_profiling(knn_index* index, int enabled);
+int knn_index_kernel_stats(knn_index* index, double* scan_ms, double* merge_ms,
+                           int64_t* scan_launches, int64_t* kernel_launches);
+int knn_index_reset_kernel_stats(knn_index* index);
+
+/* Failure-detection self-test: launches one kernel whose thread waits on a
+ * shared-memory barrier that nothing arrives on, with the engine's bounded
+ * wait limited to limit_us microseconds (1..2,000,000).  Returns
+ * KNN_ETIMEOUT when the wait gave up and reported it, as designed; the
+ * device stays usable.  No counterpart in the reference. */
+int knn_selftest_bounded_wait(int device, int64_t limit_us);
+
+/* Number of engine kernels launched since the last reset (all indices).
+ * Replaces cagra::metal_dispatch_count (cagra.hpp:119-122). */
+uint64_t knn_dispatch_count(void);
+void knn_reset_dispatch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUVS_B200_H_ */

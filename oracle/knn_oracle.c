@@ -1,0 +1,273 @@
+/*
+ * knn_oracle.c -- CPU restatement of the reference's exact L2 k-NN path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the parity checker and the timed
+ * CPU baseline ("port").  Nothing in the product library links, loads or
+ * calls it; the CUDA engine has no CPU fallback.
+ *
+ * What it restates (reference = ysys143/cuvs-silicon):
+ *   - src/cagra.cpp:211-252, the non-Apple exact search that
+ *     cuvs::neighbors::cagra::search runs when no Metal device exists:
+ *       * distance = sum over dims, in order, of (q[d] - x[d])^2 in fp32
+ *         (src/cagra.cpp:218-226);
+ *       * order by (distance ascending, index ascending)
+ *         (src/cagra.cpp:229-238);
+ *       * the first min(k, n) results are written, the rest are padded with
+ *         index UINT32_MAX and distance +inf (src/cagra.cpp:240-251).
+ *   - the same (distance, index) contract stated by the unused helper
+ *     src/metal_search.mm:12-31.
+ *
+ * The selection is a bounded max-heap rather than std::partial_sort; because
+ * (distance, index) is a total order over distinct indices, any exact
+ * selection yields the same output bytes.  The summation order of the
+ * distance is kept identical to the reference (sequential over d, fp32,
+ * no fused multiply-add: build with -ffp-contract=off), so distances are
+ * bit-identical to the reference binary built the same way.
+ *
+ * A thread-parallel entry point splits queries across POSIX threads; each
+ * query is still computed exactly as above, so results do not depend on the
+ * thread count.
+ */
+#include <math.h>
+#include <pthread.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define ORACLE_NO_INDEX 0xFFFFFFFFu
+
+/* (da, ia) is ordered after (db, ib): larger distance, or equal distance and
+ * larger index.  Mirrors the comparator at src/cagra.cpp:233-238. */
+static inline int worse(float da, uint32_t ia, float db, uint32_t ib) {
+  if (da == db) return ia > ib;
+  return da > db;
+}
+
+static void sift_down(float* hd, uint32_t* hi, int64_t size, int64_t pos) {
+  float d = hd[pos];
+  uint32_t i = hi[pos];
+  for (;;) {
+    int64_t c = 2 * pos + 1;
+    if (c >= size) break;
+    if (c + 1 < size && worse(hd[c + 1], hi[c + 1], hd[c], hi[c])) c += 1;
+    if (!worse(hd[c], hi[c], d, i)) break;
+    hd[pos] = hd[c];
+    hi[pos] = hi[c];
+    pos = c;
+  }
+  hd[pos] = d;
+  hi[pos] = i;
+}
+
+/* Exact search for one query.  heap_d / heap_i are scratch of length k. */
+static void search_one(const float* base, int64_t n, int64_t dim,
+                       const float* query, int64_t k, uint32_t* out_idx,
+                       float* out_dist, float* heap_d, uint32_t* heap_i) {
+  const int64_t take = k < n ? k : n;
+  int64_t size = 0;
+  for (int64_t v = 0; v < n; ++v) {
+    const float* x = base + v * dim;
+    float dist = 0.0f;
+    for (int64_t d = 0; d < dim; ++d) {
+      const float delta = query[d] - x[d];
+      dist += delta * delta;
+    }
+    const uint32_t idx = (uint32_t)v;
+    if (size < take) {
+      /* grow the heap: sift up */
+      int64_t pos = size++;
+      while (pos > 0) {
+        int64_t parent = (pos - 1) / 2;
+        if (!worse(dist, idx, heap_d[parent], heap_i[parent])) break;
+        heap_d[pos] = heap_d[parent];
+        heap_i[pos] = heap_i[parent];
+        pos = parent;
+      }
+      heap_d[pos] = dist;
+      heap_i[pos] = idx;
+    } else if (take > 0 && worse(heap_d[0], heap_i[0], dist, idx)) {
+      heap_d[0] = dist;
+      heap_i[0] = idx;
+      sift_down(heap_d, heap_i, size, 0);
+    }
+  }
+  /* heap sort: ascending (distance, index) */
+  for (int64_t end = size - 1; end > 0; --end) {
+    float td = heap_d[0];
+    uint32_t ti = heap_i[0];
+    heap_d[0] = heap_d[end];
+    heap_i[0] = heap_i[end];
+    heap_d[end] = td;
+    heap_i[end] = ti;
+    sift_down(heap_d, heap_i, end, 0);
+  }
+  for (int64_t r = 0; r < k; ++r) {
+    if (r < size) {
+      out_dist[r] = heap_d[r];
+      out_idx[r] = heap_i[r];
+    } else {
+      out_dist[r] = INFINITY;
+      out_idx[r] = ORACLE_NO_INDEX;
+    }
+  }
+}
+
+typedef struct {
+  const float* base;
+  int64_t n, dim;
+  const float* queries;
+  int64_t q_begin, q_end, k;
+  uint32_t* out_idx;
+  float* out_dist;
+  int status;
+} worker_arg;
+
+static void* worker(void* p) {
+  worker_arg* a = (worker_arg*)p;
+  const int64_t kk = a->k > 0 ? a->k : 1;
+  float* hd = (float*)malloc((size_t)kk * sizeof(float));
+  uint32_t* hi = (uint32_t*)malloc((size_t)kk * sizeof(uint32_t));
+  if (!hd || !hi) {
+    free(hd);
+    free(hi);
+    a->status = -1;
+    return NULL;
+  }
+  for (int64_t q = a->q_begin; q < a->q_end; ++q) {
+    search_one(a->base, a->n, a->dim, a->queries + q * a->dim, a->k,
+               a->out_idx + q * a->k, a->out_dist + q * a->k, hd, hi);
+  }
+  free(hd);
+  free(hi);
+  a->status = 0;
+  return NULL;
+}
+
+/*
+ * Exact L2 k-NN over row-major fp32 arrays.
+ * base: n x dim, queries: nq x dim, outputs: nq x k.
+ * Returns 0 on success, -1 on invalid arguments or allocation failure.
+ */
+int oracle_l2_knn(const float* base, int64_t n, int64_t dim,
+                  const float* queries, int64_t nq, int64_t k,
+                  uint32_t* out_idx, float* out_dist, int n_threads) {
+  if (n < 0 || dim <= 0 || nq < 0 || k < 0) return -1;
+  if (nq == 0 || k == 0) return 0;
+  if (!base || !queries || !out_idx || !out_dist) return -1;
+  if (n_threads < 1) n_threads = 1;
+  if (n_threads > nq) n_threads = (int)nq;
+  worker_arg* args = (worker_arg*)calloc((size_t)n_threads, sizeof(worker_arg));
+  pthread_t* th = (pthread_t*)calloc((size_t)n_threads, sizeof(pthread_t));
+  if (!args || !th) {
+    free(args);
+    free(th);
+    return -1;
+  }
+  for (int t = 0; t < n_threads; ++t) {
+    worker_arg* a = &args[t];
+    a->base = base;
+    a->n = n;
+    a->dim = dim;
+    a->queries = queries;
+    a->q_begin = nq * t / n_threads;
+    a->q_end = nq * (t + 1) / n_threads;
+    a->k = k;
+    a->out_idx = out_idx;
+    a->out_dist = out_dist;
+  }
+  int rc = 0;
+  if (n_threads == 1) {
+    worker(&args[0]);
+  } else {
+    for (int t = 0; t < n_threads; ++t) {
+      if (pthread_create(&th[t], NULL, worker, &args[t]) != 0) {
+        /* run it inline instead */
+        worker(&args[t]);
+        th[t] = 0;
+      }
+    }
+    for (int t = 0; t < n_threads; ++t)
+      if (th[t]) pthread_join(th[t], NULL);
+  }
+  for (int t = 0; t < n_threads; ++t)
+    if (args[t].status != 0) rc = -1;
+  free(args);
+  free(th);
+  return rc;
+}
+
+/*
+ * Merge per-part sorted top-k lists into one top-k list per query, with the
+ * same (distance, index) order and padding as above.  Used by the tests to
+ * check the sharded decomposition (row shards + all-gather + merge) on the
+ * CPU: lists[(q * n_parts + p) * k + r], index_offset[p] is added to every
+ * valid index of part p.
+ */
+int oracle_merge_lists(const float* list_d, const uint32_t* list_i,
+                       int64_t nq, int64_t n_parts, int64_t k,
+                       const int64_t* index_offset, uint32_t* out_idx,
+                       float* out_dist) {
+  if (nq < 0 || n_parts <= 0 || k < 0) return -1;
+  if (nq == 0 || k == 0) return 0;
+  float* hd = (float*)malloc((size_t)k * sizeof(float));
+  uint32_t* hi = (uint32_t*)malloc((size_t)k * sizeof(uint32_t));
+  if (!hd || !hi) {
+    free(hd);
+    free(hi);
+    return -1;
+  }
+  for (int64_t q = 0; q < nq; ++q) {
+    int64_t size = 0;
+    for (int64_t p = 0; p < n_parts; ++p) {
+      for (int64_t r = 0; r < k; ++r) {
+        const int64_t at = (q * n_parts + p) * k + r;
+        uint32_t idx = list_i[at];
+        if (idx == ORACLE_NO_INDEX) continue;
+        if (index_offset) idx = (uint32_t)((int64_t)idx + index_offset[p]);
+        const float dist = list_d[at];
+        if (size < k) {
+          int64_t pos = size++;
+          while (pos > 0) {
+            int64_t parent = (pos - 1) / 2;
+            if (!worse(dist, idx, hd[parent], hi[parent])) break;
+            hd[pos] = hd[parent];
+            hi[pos] = hi[parent];
+            pos = parent;
+          }
+          hd[pos] = dist;
+          hi[pos] = idx;
+        } else if (worse(hd[0], hi[0], dist, idx)) {
+          hd[0] = dist;
+          hi[0] = idx;
+          sift_down(hd, hi, size, 0);
+        }
+      }
+    }
+    for (int64_t end = size - 1; end > 0; --end) {
+      float td = hd[0];
+      uint32_t ti = hi[0];
+      hd[0] = hd[end];
+      hi[0] = hi[end];
+      hd[end] = td;
+      hi[end] = ti;
+      sift_down(hd, hi, end, 0);
+    }
+    for (int64_t r = 0; r < k; ++r) {
+      out_dist[q * k + r] = r < size ? hd[r] : INFINITY;
+      out_idx[q * k + r] = r < size ? hi[r] : ORACLE_NO_INDEX;
+    }
+  }
+  free(hd);
+  free(hi);
+  return 0;
+}
+
+/* Known-answer helper restating src/distance.cpp:8-20 (D fixed at 128). */
+float oracle_squared_l2_128(const float* lhs, const float* rhs) {
+  float distance = 0.0f;
+  for (int d = 0; d < 128; ++d) {
+    const float delta = lhs[d] - rhs[d];
+    distance += delta * delta;
+  }
+  return distance;
+}
