@@ -273,8 +273,13 @@ def run_engine(a):
     shard = gen_mixture_device(torch, a.n, lo, hi, a.dim, centres, 12, dev)
     queries = gen_mixture_device(torch, a.q, 0, a.q, a.dim, centres, 13, dev)
 
+    # all engine work and every timing event on one explicit stream (the
+    # legacy default stream's handle is 0, which the engine reads as "use
+    # the index's own stream")
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
     idx = E.Index(local)
-    stream = torch.cuda.current_stream()
     idx.set_stream(stream.cuda_stream)
     idx.build(shard, row_offset=lo, total_rows=a.n)
     torch.cuda.synchronize()

@@ -9,7 +9,7 @@
 //     one CPU thread, cached by (ptr,N,D)       (ld-padded) + norms, one kernel
 //   Q x D fp16 + q_norms on the host          queries -> device, convert kernel
 //   MPS GEMM -> Q x N fp32 in memory          fused scan kernel (TMA + tcgen05),
-//   l2_topk_from_cross (K <= 16)                Q x N stays on chip, any k<=512
+//   l2_topk_from_cross (K <= 16)                Q x N stays on chip, any k<=256
 //   copy Q x K out                            merge kernel -> caller's buffers
 //
 // Multi-GPU: one process per GPU, each index holds a contiguous row shard;
@@ -34,7 +34,7 @@
 #include <thread>
 #include <type_traits>
 
-#include "../../include/cuvs_b200.h"
+#include "cuvs_b200.h"
 #include "knn_internal.h"
 
 using knn::Plan;

@@ -21,7 +21,8 @@ constexpr int kScanThreads = 192; // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kMaxStages = 8;
 constexpr int kSmemLimit = 232448;        // sm_100 opt-in dynamic smem per CTA
 constexpr int kSmemReserve = 1024 + 256;  // 1 KiB alignment slack + barriers
-constexpr int kMaxK = 512;
+constexpr int kMaxK = 256;
+constexpr int kRowBuf = 16;       // buffered survivors per query row
 constexpr uint32_t kNoIndex = 0xFFFFFFFFu;
 
 struct ScanParams {

@@ -17,10 +17,10 @@
 //                       at a time into registers; d = |q|^2 + |x|^2 - 2 q.x
 //                       (squared L2, the expanded form of
 //                       shaders/cagra_kernels.metal:624, clamped at 0); a
-//                       per-thread threshold (the current k-th best) rejects
-//                       almost every candidate with one compare; survivors
-//                       replace the root of the thread's max-heap held in
-//                       shared memory.
+//                       per-thread threshold rejects almost every candidate
+//                       with one compare; survivors are buffered per query
+//                       and merged into the query's shared-memory max-heap
+//                       by warp-uniform flushes (see epilogue()).
 //
 // Work is split into units (query tile m, contiguous range s of dataset
 // tiles).  A persistent CTA walks units blockIdx.x, +gridDim.x, ...; at the
@@ -79,6 +79,8 @@ struct Smem {
   uint8_t* stages;
   float* heap_d;
   uint32_t* heap_i;
+  float* buf_d;
+  uint32_t* buf_i;
   uint64_t* full;
   uint64_t* empty;
   uint64_t* acc_full;
@@ -94,7 +96,9 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, const ScanParams& p) {
   s.stages = raw + pad;
   s.heap_d = reinterpret_cast<float*>(s.stages + static_cast<size_t>(p.stages) * kStageBytes);
   s.heap_i = reinterpret_cast<uint32_t*>(s.heap_d + static_cast<size_t>(p.k) * p.query_block);
-  uintptr_t b = reinterpret_cast<uintptr_t>(s.heap_i + static_cast<size_t>(p.k) * p.query_block);
+  s.buf_d = reinterpret_cast<float*>(s.heap_i + static_cast<size_t>(p.k) * p.query_block);
+  s.buf_i = reinterpret_cast<uint32_t*>(s.buf_d + static_cast<size_t>(kRowBuf) * p.query_block);
+  uintptr_t b = reinterpret_cast<uintptr_t>(s.buf_i + static_cast<size_t>(kRowBuf) * p.query_block);
   b = (b + 7) & ~static_cast<uintptr_t>(7);
   uint64_t* bars = reinterpret_cast<uint64_t*>(b);
   s.full = bars;
@@ -203,6 +207,81 @@ __device__ void mma_issuer(const ScanParams& p, const Smem& sm, uint32_t tmem_ba
   drain_wait(sm.drain, 0);
 }
 
+// Squared L2 from the fp32 dot product: |q|^2 + |x|^2 - 2 q.x, clamped at 0.
+// Used by every pass over a tile so all passes see identical values.
+__device__ __forceinline__ float l2_from_dot(uint32_t acc_bits, float qn, float xn) {
+  const float d = fmaf(-2.0f, __uint_as_float(acc_bits), qn + xn);
+  return d < 0.0f ? 0.0f : d;
+}
+
+// Ascending sort of 32 registers: bitonic network with every index a
+// template constant, so the array stays in registers.
+template <int Size, int Stride>
+__device__ __forceinline__ void bitonic_pass(float (&g)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int j = i ^ Stride;
+    if (j > i) {
+      const float a = g[i], b = g[j];
+      const bool up = (i & Size) == 0;
+      g[i] = up ? fminf(a, b) : fmaxf(a, b);
+      g[j] = up ? fmaxf(a, b) : fminf(a, b);
+    }
+  }
+  if constexpr (Stride > 1) bitonic_pass<Size, Stride / 2>(g);
+}
+
+template <int Size>
+__device__ __forceinline__ void bitonic_sort(float (&g)[32]) {
+  bitonic_pass<Size, Size / 2>(g);
+  if constexpr (Size < 32) bitonic_sort<Size * 2>(g);
+}
+
+__device__ __forceinline__ void sort32(float (&g)[32]) { bitonic_sort<2>(g); }
+
+// Per query row (one epilogue lane): the filter threshold, the heap root
+// and the number of buffered survivors.
+struct RowState {
+  float thr;   // candidates with d < thr are kept
+  float rd;    // heap root (worst kept) distance and index
+  uint32_t ri;
+  int cnt;     // survivors waiting in the row's buffer
+};
+
+// Moves every lane's buffered survivors into its heap.  Warp-uniform: all
+// lanes run the same number of iterations (the warp's largest buffer), so
+// the heap updates of the 32 query rows proceed in lock-step.
+__device__ __forceinline__ void flush_buffer(RowState& st, const Smem& sm, int k, int stride,
+                                             int row) {
+  const int maxc = __reduce_max_sync(0xffffffffu, st.cnt);
+  for (int b = 0; b < maxc; ++b) {
+    if (b < st.cnt) {
+      const float d = sm.buf_d[b * stride + row];
+      const uint32_t i = sm.buf_i[b * stride + row];
+      if (d < st.rd || (d == st.rd && i < st.ri)) {
+        heap_sift_down(sm.heap_d, sm.heap_i, k, stride, row, 0, d, i);
+        st.rd = sm.heap_d[row];
+        st.ri = sm.heap_i[row];
+      }
+    }
+  }
+  st.cnt = 0;
+  st.thr = fminf(st.thr, st.rd);
+}
+
+// Epilogue warp.  Lane `row` owns query row `row` of the unit's query block.
+//
+// Candidate handling per 32-column chunk of an accumulator tile:
+//   * d for the 32 columns in registers; survivors are d < thr (one compare);
+//   * survivors are appended to the row's shared-memory buffer (kRowBuf);
+//   * when any lane's buffer could overflow, the whole warp flushes its
+//     buffers into the heaps (flush_buffer) and tightens thr.
+// Seeding: on the first tile of a unit (k <= 32) a first pass over the tile
+// takes the minimum of each column position j over the 8 chunks (32 group
+// minima, each the distance of a distinct row); the k-th smallest of them,
+// t, has at least k rows of this unit at d <= t, so the unit's k-th best is
+// <= t and filtering with d <= t drops no result.  This keeps the first
+// tile from pushing all 256 columns through the heap.
 __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base, int warp,
                          int lane) {
   const int quad = warp & 3;              // TMEM lane quadrant this warp may access
@@ -210,6 +289,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
   const bool warp_active = quad * 32 < p.query_block;
   const int stride = p.query_block;
   const int k = p.k;
+  const float kInf = __int_as_float(0x7f800000);
   uint32_t tc = 0;
   bool failed = false;
   for (int u = blockIdx.x; u < p.units && !failed; u += gridDim.x) {
@@ -221,11 +301,15 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
     const float qn = valid_q ? p.query_norms[q] : 0.0f;
     if (valid_q) {
       for (int pos = 0; pos < k; ++pos) {
-        sm.heap_d[pos * stride + row] = __int_as_float(0x7f800000);
+        sm.heap_d[pos * stride + row] = kInf;
         sm.heap_i[pos * stride + row] = kNoIndex;
       }
     }
-    float thr = valid_q ? __int_as_float(0x7f800000) : __int_as_float(0xff800000);
+    RowState st;
+    st.thr = valid_q ? kInf : __int_as_float(0xff800000);
+    st.rd = kInf;
+    st.ri = kNoIndex;
+    st.cnt = 0;
     for (int64_t t = t0; t < t1; ++t) {
       const uint32_t b = tc & 1u;
       // every lane waits; the warp leaves together if any lane gave up, so
@@ -238,31 +322,61 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
       tc_fence_after();
       if (warp_active) {
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + b * kAccCols;
+        if (t == t0 && k <= 32) {
+          float g[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) g[j] = kInf;
+#pragma unroll 1
+          for (int c = 0; c < kAccCols / 32; ++c) {
+            const int64_t col = t * kTileRows + c * 32 + lane;
+            const float xn = col < p.n_rows ? __ldg(p.row_norms + col) : kInf;
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tbase + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              g[j] = fminf(g[j], l2_from_dot(r[j], qn, __shfl_sync(0xffffffffu, xn, j)));
+          }
+          sort32(g);
+          // g is ascending, so g[k - 1] = max of g[0..k-1] (written without a
+          // run-time register index)
+          float tk = g[0];
+#pragma unroll
+          for (int j = 1; j < 32; ++j) tk = fmaxf(tk, j < k ? g[j] : 0.0f);
+          // keep d <= tk: the next float up (tk >= 0 here)
+          if (valid_q && tk < kInf) st.thr = fminf(st.thr, __int_as_float(__float_as_int(tk) + 1));
+        }
 #pragma unroll 1
         for (int c = 0; c < kAccCols / 32; ++c) {
           // row norm of column (c * 32 + lane); its load overlaps the TMEM load
           const int64_t col = t * kTileRows + c * 32 + lane;
-          const float xn = col < p.n_rows ? __ldg(p.row_norms + col) : __int_as_float(0x7f800000);
+          const float xn = col < p.n_rows ? __ldg(p.row_norms + col) : kInf;
           uint32_t r[32];
           tmem_ld_32x32b_x32(tbase + c * 32, r);
           tmem_ld_wait();
           float dv[32];
-          uint32_t mask = 0;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float xj = __shfl_sync(0xffffffffu, xn, j);
-            float d = fmaf(-2.0f, __uint_as_float(r[j]), qn + xj);
-            d = d < 0.0f ? 0.0f : d;
-            dv[j] = d;
-            mask |= (d < thr ? 1u : 0u) << j;
-          }
-          if (mask) {
-            const uint32_t col0 = static_cast<uint32_t>(t * kTileRows + c * 32);
+          for (int j = 0; j < 32; ++j) dv[j] = l2_from_dot(r[j], qn, __shfl_sync(0xffffffffu, xn, j));
+          const uint32_t col0 = static_cast<uint32_t>(t * kTileRows + c * 32);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (((mask >> j) & 1u) && dv[j] < thr) {
-                heap_sift_down(sm.heap_d, sm.heap_i, k, stride, row, 0, dv[j], col0 + j);
-                thr = sm.heap_d[row];
+          for (int h = 0; h < 32; h += kRowBuf) {
+            uint32_t mask = 0;
+#pragma unroll
+            for (int j = 0; j < kRowBuf; ++j) mask |= (dv[h + j] < st.thr ? 1u : 0u) << j;
+            if (__any_sync(0xffffffffu, mask != 0)) {
+              if (__any_sync(0xffffffffu, st.cnt + __popc(mask) > kRowBuf)) {
+                flush_buffer(st, sm, k, stride, row);
+                mask = 0;
+#pragma unroll
+                for (int j = 0; j < kRowBuf; ++j) mask |= (dv[h + j] < st.thr ? 1u : 0u) << j;
+              }
+#pragma unroll
+              for (int j = 0; j < kRowBuf; ++j) {
+                if ((mask >> j) & 1u) {
+                  sm.buf_d[st.cnt * stride + row] = dv[h + j];
+                  sm.buf_i[st.cnt * stride + row] = col0 + h + j;
+                  ++st.cnt;
+                }
               }
             }
           }
@@ -274,6 +388,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
       ++tc;
     }
     if (failed) break;
+    if (warp_active) flush_buffer(st, sm, k, stride, row);
     if (valid_q) {
       // heap sort -> ascending (distance, index)
       for (int end = k - 1; end > 0; --end) {
@@ -370,7 +485,7 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
   if (n_rows <= 0 || dim <= 0 || n_queries <= 0 || k <= 0 || !out) return 1;
   if (k > kMaxK) return 6;
   if (num_sms <= 0) num_sms = 148;
-  const int64_t heap_per_query = k * 8;
+  const int64_t heap_per_query = (k + kRowBuf) * 8;  // heap + survivor buffer
   const int64_t budget = kSmemLimit - kSmemReserve;
   int64_t qb_cap = (budget - 2 * kStageBytes) / heap_per_query;
   qb_cap = (qb_cap / 32) * 32;

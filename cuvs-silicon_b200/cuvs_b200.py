@@ -40,7 +40,7 @@ DTYPE_F16 = 1
 METRIC_L2_EXPANDED = 0
 METRIC_INNER_PRODUCT = 1
 NO_INDEX = 0xFFFFFFFF
-MAX_K = 512
+MAX_K = 256
 
 
 class KnnPlan(ctypes.Structure):

@@ -63,9 +63,9 @@ extern "C" {
 #define KNN_METRIC_INNER_PRODUCT 1
 
 /* Largest k one search accepts (per-CTA top-k state must fit in shared
- * memory next to a two-stage pipeline).  The reference's Metal kernel caps k
+ * memory next to a two-stage pipeline and a survivor buffer).  The reference's Metal kernel caps k
  * at 16 (shaders/cagra_kernels.metal:538); its CPU path has no cap. */
-#define KNN_MAX_K 512
+#define KNN_MAX_K 256
 
 /* UINT32_MAX marks "no neighbour" (src/cagra.cpp:248-249). */
 #define KNN_NO_INDEX 0xFFFFFFFFu

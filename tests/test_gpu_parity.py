@@ -110,7 +110,8 @@ SHAPES = [
     (3000, 72, 300, 32),
     (4099, 256, 16, 256),
     (2500, 128, 100, 256),
-    (1500, 64, 40, 512),
+    (1500, 64, 40, 200),
+    (700, 64, 300, 100),
 ]
 
 
@@ -123,6 +124,16 @@ def test_random_shapes(engine, oracle_mod, torch_cuda, n, dim, nq, k):
     b16, q16, oi, od = _check(oracle_mod, base, queries, k)
     par = oracle_mod.check_parity(b16, q16, i, d, oi, od, REL_TOL)
     assert par.ok, par.detail
+
+
+def test_identical_rows_tie_by_index(engine, oracle_mod, torch_cuda):
+    """Every row at the same distance: the first-tile threshold seed equals
+    that distance, and the result must be rows 0..k-1 in index order."""
+    base = np.tile(np.arange(64, dtype=np.float32) / 64, (3000, 1))
+    queries = np.zeros((3, 64), np.float32)
+    i, d = _search(engine, base, queries, 10)
+    assert i.tolist() == [list(range(10))] * 3
+    assert np.all(d == d[0, 0])
 
 
 def test_c2_mixture(engine, oracle_mod, torch_cuda):
@@ -207,7 +218,7 @@ def test_argument_errors(engine, torch_cuda):
         with pytest.raises(ValueError, match="dimension"):
             idx.search(np.ones((2, 5), np.float32), 2)
         with pytest.raises(RuntimeError, match="UNSUPPORTED"):
-            idx.search(np.ones((2, 4), np.float32), 513)
+            idx.search(np.ones((2, 4), np.float32), 257)
         i, d = idx.search(np.ones((0, 4), np.float32), 3)   # no-op
         assert i.shape == (0, 3)
         i, d = idx.search(np.ones((2, 4), np.float32), 0)   # k = 0: no-op
