@@ -745,3 +745,141 @@ uint64_t knn_dispatch_count(void) { return g_dispatch.load(); }
 void knn_reset_dispatch_count(void) { g_dispatch.store(0); }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Search without allocation (knn_index_search_noalloc).
+//
+// For callers that must not allocate device memory while they search: code
+// that runs under a memory pool or budget owned by someone else (a serving
+// framework that has pre-reserved the GPU), code that must not trigger the
+// implicit device synchronisation cudaMalloc/cudaFree can cause, or code
+// that runs where allocation is forbidden outright.  The per-search scratch
+// (fp16 queries, query norms, per-unit top-k lists, and host staging when
+// the caller passes host buffers) lives in one file-scope device array of
+// KNN_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until
+// the process exits.  The index itself must already be built.
+//
+// Host code cannot use the array's name as a device address: the address is
+// taken with cudaGetSymbolAddress once per device, with that device
+// current, on the first call of this entry point on that device; make that
+// first call before any stream capture.
+//
+// Every call on a device shares the one array and it keeps the previous
+// call's contents.  Nothing in it needs clearing: each kernel overwrites
+// every scratch byte that a later kernel reads (every query row, every
+// (query, split, rank) list entry).  Calls through this entry point on the
+// same device are serialised by a host lock and each call blocks until its
+// results are in place; work that overlaps on the GPU with a call of this
+// entry point and also uses this array (for instance from another thread
+// that bypasses the call) would race.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[KNN_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu[kNoAllocMaxDevices];
+void* g_noalloc_base[kNoAllocMaxDevices] = {};
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
+                   uint32_t* neighbors, float* distances) {
+  int st = validate_search(h, queries, nq, k, neighbors, distances);
+  if (st != KNN_OK || nq == 0 || k == 0) return st;
+  if (h->comm) return fail(KNN_EUNSUPPORTED, "the no-allocation search does not run on a communicator");
+  if (h->device < 0 || h->device >= kNoAllocMaxDevices)
+    return fail(KNN_EUNSUPPORTED, "device %d beyond the no-allocation table", h->device);
+  std::lock_guard<std::mutex> dev_lock(g_noalloc_mu[h->device]);
+  std::lock_guard<std::mutex> lock(h->mu);
+  KNN_CUDA(cudaSetDevice(h->device));
+  if (!g_noalloc_base[h->device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(KNN_ECUDA, "cudaGetSymbolAddress(no-allocation scratch): %s",
+                  cudaGetErrorString(e));
+    g_noalloc_base[h->device] = p;
+  }
+  unsigned char* base = static_cast<unsigned char*>(g_noalloc_base[h->device]);
+
+  const int cq = classify(queries, h->device);
+  const int cn = classify(neighbors, h->device);
+  const int cd = classify(distances, h->device);
+  if (cq < 0 || cn < 0 || cd < 0)
+    return fail(KNN_EINVAL, "buffer lives on a different device than the index");
+
+  Plan plan;
+  const int pst = knn::plan_search(h->n, h->dim, nq, k, h->num_sms, &plan);
+  if (pst != 0) return fail(pst, "k = %lld is outside the engine's limits", (long long)k);
+
+  // carve the scratch array
+  const size_t qk = static_cast<size_t>(nq) * k;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    unsigned char* p = base + off;
+    off += align256(bytes);
+    return p;
+  };
+  __half* q16 = reinterpret_cast<__half*>(take(static_cast<size_t>(nq) * h->ld * 2));
+  float* qnorm = reinterpret_cast<float*>(take(static_cast<size_t>(nq) * 4));
+  float* part_d = reinterpret_cast<float*>(take(static_cast<size_t>(plan.partial_bytes / 2)));
+  uint32_t* part_i = reinterpret_cast<uint32_t*>(take(static_cast<size_t>(plan.partial_bytes / 2)));
+  float* q32 = cq == 0 ? reinterpret_cast<float*>(take(static_cast<size_t>(nq) * h->dim * 4)) : nullptr;
+  float* out_d = cd == 0 ? reinterpret_cast<float*>(take(qk * 4)) : distances;
+  uint32_t* out_i = cn == 0 ? reinterpret_cast<uint32_t*>(take(qk * 4)) : neighbors;
+  if (off > static_cast<size_t>(KNN_NOALLOC_SCRATCH_BYTES))
+    return fail(KNN_EUNSUPPORTED,
+                "search needs %zu bytes of scratch; the no-allocation search has %d "
+                "(use fewer queries or a smaller k, or knn_index_search)",
+                off, KNN_NOALLOC_SCRATCH_BYTES);
+
+  const float* qsrc = queries;
+  if (cq == 0) {
+    KNN_CUDA(cudaMemcpyAsync(q32, queries, static_cast<size_t>(nq) * h->dim * 4,
+                             cudaMemcpyHostToDevice, h->stream));
+    qsrc = q32;
+  }
+  KNN_CUDA(knn::launch_convert_rows(qsrc, false, nq, h->dim, q16, h->ld, qnorm, h->stream));
+  CUtensorMap qmap;
+  if ((st = encode_rows(&qmap, q16, nq, h->ld, knn::kQueryRows)) != KNN_OK) return st;
+
+  knn::ScanParams p;
+  p.row_norms = h->norms;
+  p.query_norms = qnorm;
+  p.part_d = part_d;
+  p.part_i = part_i;
+  p.err = h->err_dev;
+  p.n_rows = h->n;
+  p.n_queries = nq;
+  p.row_tiles = plan.row_tiles;
+  p.k = static_cast<int32_t>(k);
+  p.query_block = static_cast<int32_t>(plan.query_block);
+  p.query_tiles = static_cast<int32_t>(plan.query_tiles);
+  p.splits = static_cast<int32_t>(plan.splits);
+  p.units = static_cast<int32_t>(plan.units);
+  p.k_chunks = static_cast<int32_t>((h->ld + knn::kKChunk - 1) / knn::kKChunk);
+  p.stages = static_cast<int32_t>(plan.stages);
+  p.dataset_evict_first = plan.query_tiles == 1 ? 1 : 0;
+  KNN_CUDA(knn::launch_scan(qmap, h->xmap, p, plan, h->stream));
+  KNN_CUDA(knn::launch_merge(part_d, part_i, k, plan.splits * k, static_cast<int>(plan.splits),
+                             static_cast<int>(k), nq, h->row_offset, out_d, out_i, false,
+                             h->stream));
+  if (cd == 0)
+    KNN_CUDA(cudaMemcpyAsync(distances, out_d, qk * 4, cudaMemcpyDeviceToHost, h->stream));
+  if (cn == 0)
+    KNN_CUDA(cudaMemcpyAsync(neighbors, out_i, qk * 4, cudaMemcpyDeviceToHost, h->stream));
+  g_dispatch.fetch_add(3);
+  h->kernel_launches += 3;
+  h->scan_launches += 1;
+  KNN_CUDA(cudaMemcpyAsync(h->err_host, h->err_dev, sizeof(int), cudaMemcpyDeviceToHost,
+                           h->stream));
+  KNN_CUDA(cudaStreamSynchronize(h->stream));
+  return check_device_error(h);
+}
+
+}  // namespace
+
+extern "C" int knn_index_search_noalloc(knn_index* h, const float* queries, int64_t nq,
+                                        int64_t k, uint32_t* neighbors, float* distances) {
+  return noalloc_search(h, queries, nq, k, neighbors, distances);
+}

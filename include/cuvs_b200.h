@@ -141,6 +141,28 @@ int knn_index_search_i64(knn_index* index, const float* queries,
                          int64_t n_queries, int64_t k, int64_t* neighbors,
                          float* distances);
 
+/* Size of the device scratch array used by knn_index_search_noalloc. */
+#define KNN_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
+
+/* knn_index_search without allocating: same arguments, same results, same
+ * blocking behaviour.  No counterpart in the reference.  It is for callers
+ * that cannot call cudaMalloc while they search: a serving process whose
+ * device memory is owned by another allocator or budget, or code that must
+ * not risk the device-wide synchronisation that cudaMalloc/cudaFree may
+ * cause.  Its per-search scratch is one static device array of
+ * KNN_NOALLOC_SCRATCH_BYTES (16 MiB) that every GPU loading the library
+ * holds until exit.  A search whose scratch (fp16 queries, norms, per-split
+ * top-k lists, staging of host buffers) exceeds it fails with
+ * KNN_EUNSUPPORTED; the headline search (100 queries, k = 10, dim 1024)
+ * needs about 2 MiB.  The first call on a device looks up the array's
+ * device address, so make it before any stream capture.  Calls share the
+ * array: concurrent calls on one device are serialised by the library; other
+ * work that overlaps them on the GPU and touches the array would race.
+ * The index must be built, and no communicator may be attached. */
+int knn_index_search_noalloc(knn_index* index, const float* queries,
+                             int64_t n_queries, int64_t k, uint32_t* neighbors,
+                             float* distances);
+
 /* Stream-ordered search: all four pointers must be device memory; returns
  * after enqueueing on the index's stream without synchronising.  Errors
  * raised by the kernels themselves (bounded-wait timeouts) are reported by
