@@ -33,6 +33,7 @@
 #include <string>
 #include <thread>
 #include <type_traits>
+#include <vector>
 
 #include "cuvs_b200.h"
 #include "knn_internal.h"
@@ -594,6 +595,39 @@ int knn_index_build(knn_index* h, const void* rows, int dtype, int64_t n, int64_
 int knn_index_build_shard(knn_index* h, const void* rows, int dtype, int64_t n, int64_t dim,
                           int metric, int64_t row_offset, int64_t total_rows) {
   return build_impl(h, rows, dtype, n, dim, metric, row_offset, total_rows);
+}
+
+int knn_index_copy_rows(knn_index* h, void* out, int dtype) {
+  if (!h || !out) return fail(KNN_EINVAL, "null index or output");
+  if (!h->data) return fail(KNN_EINVAL, "index has no dataset");
+  if (dtype != KNN_DTYPE_F16 && dtype != KNN_DTYPE_F32) return fail(KNN_EINVAL, "unknown dtype");
+  std::lock_guard<std::mutex> lock(h->mu);
+  KNN_CUDA(cudaSetDevice(h->device));
+  const int where = classify(out, h->device);
+  if (where < 0) return fail(KNN_EINVAL, "output lives on a different device than the index");
+  if (dtype == KNN_DTYPE_F16) {
+    KNN_CUDA(cudaMemcpy2DAsync(out, static_cast<size_t>(h->dim) * 2, h->data,
+                               static_cast<size_t>(h->ld) * 2, static_cast<size_t>(h->dim) * 2,
+                               static_cast<size_t>(h->n), cudaMemcpyDefault, h->stream));
+    KNN_CUDA(cudaStreamSynchronize(h->stream));
+    return KNN_OK;
+  }
+  if (where == 1) return fail(KNN_EINVAL, "fp32 rows can only be copied to host memory");
+  // widen chunk by chunk through a pinned-free host bounce buffer
+  const int64_t chunk = std::max<int64_t>(1, (int64_t(64) << 20) / (h->dim * 2));
+  std::vector<__half> tmp(static_cast<size_t>(std::min(chunk, h->n) * h->dim));
+  float* dst = static_cast<float*>(out);
+  for (int64_t r0 = 0; r0 < h->n; r0 += chunk) {
+    const int64_t rr = std::min(chunk, h->n - r0);
+    KNN_CUDA(cudaMemcpy2DAsync(tmp.data(), static_cast<size_t>(h->dim) * 2,
+                               h->data + static_cast<size_t>(r0) * h->ld,
+                               static_cast<size_t>(h->ld) * 2, static_cast<size_t>(h->dim) * 2,
+                               static_cast<size_t>(rr), cudaMemcpyDeviceToHost, h->stream));
+    KNN_CUDA(cudaStreamSynchronize(h->stream));
+    for (int64_t i = 0; i < rr * h->dim; ++i)
+      dst[static_cast<size_t>(r0 * h->dim + i)] = __half2float(tmp[static_cast<size_t>(i)]);
+  }
+  return KNN_OK;
 }
 
 int64_t knn_index_rows(const knn_index* h) { return h ? h->n : 0; }

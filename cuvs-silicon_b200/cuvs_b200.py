@@ -72,6 +72,7 @@ def lib() -> ctypes.CDLL:
         "knn_index_build_shard": (I, [P, P, I, I64, I64, I, I64, I64]),
         "knn_index_rows": (I64, [P]),
         "knn_index_dim": (I64, [P]),
+        "knn_index_copy_rows": (I, [P, P, I]),
         "knn_index_search": (I, [P, P, I64, I64, P, P]),
         "knn_index_search_i64": (I, [P, P, I64, I64, P, P]),
         "knn_index_search_async": (I, [P, P, I64, I64, P, P]),
@@ -201,6 +202,13 @@ class Index:
     @property
     def dim(self) -> int:
         return int(lib().knn_index_dim(self._h))
+
+    def copy_rows(self, dtype=np.float32) -> np.ndarray:
+        """The stored (fp16-rounded) rows, as a host array."""
+        out = np.empty((self.rows, self.dim), dtype=dtype)
+        code = DTYPE_F32 if out.dtype == np.float32 else DTYPE_F16
+        _check(lib().knn_index_copy_rows(self._h, ctypes.c_void_p(out.ctypes.data), code))
+        return out
 
     def set_stream(self, stream_handle: int | None) -> None:
         _check(lib().knn_index_set_stream(self._h, ctypes.c_void_p(stream_handle or 0)))

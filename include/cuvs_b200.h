@@ -123,6 +123,13 @@ int knn_index_build_shard(knn_index* index, const void* rows, int dtype,
 int64_t knn_index_rows(const knn_index* index);
 int64_t knn_index_dim(const knn_index* index);
 
+/* Copies the index's stored rows (n_rows x dim, row-major, the fp16 values
+ * the engine searches) into `out`: dtype KNN_DTYPE_F16 to host or device
+ * memory, KNN_DTYPE_F32 (exact widening) to host memory.  Used to save an
+ * index in the reference's container (src/cagra.cpp:305-328 writes the
+ * dataset as fp32). */
+int knn_index_copy_rows(knn_index* index, void* out, int dtype);
+
 /* Exact k-NN of n_queries fp32 queries (host or device, row-major, index
  * dim columns).  Writes neighbours (uint32) and squared distances (fp32),
  * each n_queries x k, ascending by (distance, index); slots beyond the

@@ -1,0 +1,102 @@
+"""Worker for the multi-rank tests (one process per rank, launched by
+torch.distributed.run).  Modes:
+
+  cpu-merge   gloo only, no GPU: each rank takes its row shard
+              (knn_shard_range of the C ABI), searches it with the oracle,
+              all-gathers the per-rank (distance, index) lists and merges
+              them; the result must equal the oracle on the full dataset.
+  cpu-lost    gloo only: rank 1 leaves before the collective; rank 0 must
+              get an error from its all-gather within the short timeout
+              instead of hanging.
+  gpu         one GPU per rank: row shards built with global offsets,
+              NCCL communicator attached, every rank searches and receives
+              the merged global result, checked against the oracle.
+Exit code 0 = pass.
+"""
+import datetime
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+sys.path.insert(0, os.path.join(ROOT, "cuvs-silicon_b200"))
+
+
+def main():
+    import torch
+    import torch.distributed as dist
+
+    mode = sys.argv[1]
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    timeout = datetime.timedelta(seconds=8 if mode == "cpu-lost" else 120)
+    dist.init_process_group("gloo", timeout=timeout)
+
+    import cuvs_b200 as E
+    import oracle as O
+
+    n, dim, nq = 20011, 72, 37
+    base = O.gen_iid(n, dim, 101)
+    queries = O.gen_iid(nq, dim, 102)
+    b16, q16 = O.round_fp16(base), O.round_fp16(queries)
+    lo, hi = E.shard_range(n, world, rank)
+
+    if mode == "cpu-merge":
+        for k in (1, 10, 50):
+            li, ld = O.port_knn(b16[lo:hi], q16, k)
+            li = np.where(li == O.NO_INDEX, li, li + lo).astype(np.uint32)
+            gi = [torch.empty((nq, k), dtype=torch.int64) for _ in range(world)]
+            gd = [torch.empty((nq, k), dtype=torch.float32) for _ in range(world)]
+            dist.all_gather(gi, torch.from_numpy(li.astype(np.int64)))
+            dist.all_gather(gd, torch.from_numpy(ld))
+            lists_i = np.stack([g.numpy().astype(np.uint32) for g in gi], axis=1)
+            lists_d = np.stack([g.numpy() for g in gd], axis=1)
+            mi, md = O.merge_lists(lists_d, lists_i)
+            fi, fd = O.port_knn(b16, q16, k)
+            assert np.array_equal(mi, fi) and np.array_equal(md, fd), f"k={k}"
+        dist.barrier()
+        dist.destroy_process_group()
+        return 0
+
+    if mode == "cpu-lost":
+        if rank == 1:
+            os._exit(0)  # leaves between steps, nothing in flight
+        try:
+            dist.all_gather([torch.empty(4) for _ in range(world)], torch.zeros(4))
+        except Exception as e:  # the loss is detected on the host
+            print(f"rank 0 detected the lost peer: {type(e).__name__}", flush=True)
+            return 0
+        print("rank 0: collective completed without its peer", flush=True)
+        return 1
+
+    if mode == "gpu":
+        torch.cuda.set_device(rank)
+        obj = [E.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        with E.Index(rank) as idx:
+            idx.build(base[lo:hi], row_offset=lo, total_rows=n)
+            idx.attach_comm(obj[0], world, rank)
+            for k in (1, 10, 100, 256):
+                gi, gd = idx.search(queries, k)
+                oi, od = O.port_knn(b16, q16, k, threads=4)
+                par = O.check_parity(b16, q16, gi, gd, oi, od, 1e-3)
+                assert par.ok, f"rank {rank} k={k}: {par.detail}"
+            # stream-ordered path with device buffers, twice
+            qd = torch.from_numpy(queries).cuda()
+            ni = torch.empty((nq, 10), dtype=torch.int32, device="cuda")
+            nd = torch.empty((nq, 10), dtype=torch.float32, device="cuda")
+            ref_i, _ = idx.search(queries, 10)
+            for _ in range(2):
+                idx.search_async(qd, 10, ni, nd)
+                idx.sync()
+                assert np.array_equal(ni.cpu().numpy().view(np.uint32), ref_i)
+        dist.barrier()
+        dist.destroy_process_group()
+        return 0
+    raise SystemExit(f"unknown mode {mode}")
+
+
+if __name__ == "__main__":
+    sys.exit(main())
