@@ -29,7 +29,7 @@
 // reduces the lists to the final top-k, ordered by (distance, index) like
 // src/cagra.cpp:229-238.
 //
-// No TMA multicast is used anywhere (the same code runs under multi-GPU
+// Every TMA load lands in the issuing CTA only (the same code runs under multi-GPU
 // sharding).  Every mbarrier wait is bounded (ptx.cuh).
 #include <cuda.h>
 #include <cuda_runtime.h>

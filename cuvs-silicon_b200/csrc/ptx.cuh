@@ -109,7 +109,7 @@ __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
                : "memory");
 }
 
-// 2-D tiled load (no multicast).  x = innermost coordinate (elements; a
+// 2-D tiled load into this CTA only.  x = innermost coordinate (elements; a
 // multiple of 64 here, i.e. 128-byte aligned), y = row.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map,
                                             uint64_t* bar, int32_t x, int32_t y,
