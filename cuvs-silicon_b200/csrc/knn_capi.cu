@@ -24,6 +24,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <array>
 #include <atomic>
 #include <chrono>
 #include <cstdarg>
@@ -219,9 +220,12 @@ struct knn_index {
   ncclComm_t comm = nullptr;
   int n_ranks = 1, rank = 0;
 
-  // profiling
+  // profiling: one (before scan, after scan, after merge) event triple per
+  // search, read back when the stats are requested
   bool profiling = false;
   cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+  std::vector<std::array<cudaEvent_t, 3>> prof_events;
+  size_t prof_used = 0;
   double scan_ms = 0.0, merge_ms = 0.0;
   int64_t scan_launches = 0, kernel_launches = 0;
 };
@@ -277,6 +281,37 @@ int sync_stream(knn_index* h) {
   }
 }
 
+// Adds the durations of the recorded event triples (the stream must be idle).
+int drain_profile(knn_index* h) {
+  for (size_t i = 0; i < h->prof_used; ++i) {
+    float a = 0.f, b = 0.f;
+    KNN_CUDA(cudaEventElapsedTime(&a, h->prof_events[i][0], h->prof_events[i][1]));
+    KNN_CUDA(cudaEventElapsedTime(&b, h->prof_events[i][1], h->prof_events[i][2]));
+    h->scan_ms += a;
+    h->merge_ms += b;
+  }
+  h->prof_used = 0;
+  return KNN_OK;
+}
+
+// Returns the next free event triple (synchronising and draining when the
+// pool is full).
+int next_profile_slot(knn_index* h, std::array<cudaEvent_t, 3>** out) {
+  constexpr size_t kMaxPending = 4096;
+  if (h->prof_used == kMaxPending) {
+    KNN_CUDA(cudaStreamSynchronize(h->stream));
+    int st = drain_profile(h);
+    if (st != KNN_OK) return st;
+  }
+  if (h->prof_used == h->prof_events.size()) {
+    std::array<cudaEvent_t, 3> t{};
+    for (auto& e : t) KNN_CUDA(cudaEventCreate(&e));
+    h->prof_events.push_back(t);
+  }
+  *out = &h->prof_events[h->prof_used++];
+  return KNN_OK;
+}
+
 int check_device_error(knn_index* h) {
   if (*h->err_host != 0) {
     const int code = *h->err_host;
@@ -324,7 +359,8 @@ int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void*
 
   // scratch
   const size_t qk = static_cast<size_t>(nq) * k;
-  if ((st = h->q16.ensure(static_cast<size_t>(nq) * h->ld * 2)) != KNN_OK) return st;
+  const int64_t nq_pad = knn::padded_query_rows(plan);
+  if ((st = h->q16.ensure(static_cast<size_t>(nq_pad) * h->ld * 2)) != KNN_OK) return st;
   if ((st = h->qnorm.ensure(static_cast<size_t>(nq) * 4)) != KNN_OK) return st;
   if ((st = h->part_d.ensure(static_cast<size_t>(plan.partial_bytes / 2))) != KNN_OK) return st;
   if ((st = h->part_i.ensure(static_cast<size_t>(plan.partial_bytes / 2))) != KNN_OK) return st;
@@ -336,11 +372,11 @@ int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void*
                              cudaMemcpyHostToDevice, h->stream));
     qsrc = h->q32.as<float>();
   }
-  KNN_CUDA(knn::launch_convert_rows(qsrc, false, nq, h->dim, h->q16.as<__half>(), h->ld,
-                                    h->qnorm.as<float>(), h->stream));
+  KNN_CUDA(knn::launch_convert_rows(qsrc, false, nq, nq_pad, h->dim, h->q16.as<__half>(),
+                                    h->ld, h->qnorm.as<float>(), h->stream));
 
   CUtensorMap qmap;
-  if ((st = encode_rows(&qmap, h->q16.as<__half>(), nq, h->ld, knn::kQueryRows)) != KNN_OK)
+  if ((st = encode_rows(&qmap, h->q16.as<__half>(), nq_pad, h->ld, knn::kQueryRows)) != KNN_OK)
     return st;
 
   knn::ScanParams p;
@@ -361,9 +397,15 @@ int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void*
   p.stages = static_cast<int32_t>(plan.stages);
   p.dataset_evict_first = plan.query_tiles == 1 ? 1 : 0;
 
-  if (h->profiling) KNN_CUDA(cudaEventRecord(h->ev[0], h->stream));
-  KNN_CUDA(knn::launch_scan(qmap, h->xmap, p, plan, h->stream));
-  if (h->profiling) KNN_CUDA(cudaEventRecord(h->ev[1], h->stream));
+  std::array<cudaEvent_t, 3>* prof = nullptr;
+  if (h->profiling) {
+    if ((st = next_profile_slot(h, &prof)) != KNN_OK) return st;
+    KNN_CUDA(cudaEventRecord((*prof)[0], h->stream));
+  }
+  // with timing events between kernels, launch them plainly serialised
+  const bool overlap = prof == nullptr;
+  KNN_CUDA(knn::launch_scan(qmap, h->xmap, p, plan, h->stream, overlap));
+  if (prof) KNN_CUDA(cudaEventRecord((*prof)[1], h->stream));
 
   // destination of the merged result
   const size_t idx_bytes = qk * (out_i64 ? 8 : 4);
@@ -382,7 +424,7 @@ int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void*
   if (!h->comm) {
     KNN_CUDA(knn::launch_merge(p.part_d, p.part_i, k, plan.splits * k,
                                static_cast<int>(plan.splits), static_cast<int>(k), nq,
-                               h->row_offset, dst_d, dst_i, out_i64, h->stream));
+                               h->row_offset, dst_d, dst_i, out_i64, h->stream, overlap));
     launches += 1;
   } else {
     // local merge into the send buffer: [dist k floats | idx k uint32] per query
@@ -393,7 +435,7 @@ int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void*
     uint32_t* send_i = reinterpret_cast<uint32_t*>(send_d + qk);
     KNN_CUDA(knn::launch_merge(p.part_d, p.part_i, k, plan.splits * k,
                                static_cast<int>(plan.splits), static_cast<int>(k), nq,
-                               h->row_offset, send_d, send_i, false, h->stream));
+                               h->row_offset, send_d, send_i, false, h->stream, overlap));
     ncclResult_t r = nccl().AllGather(h->gather_send.ptr, h->gather_recv.ptr, list_bytes,
                                    ncclUint8, h->comm, h->stream);
     if (r == ncclInProgress) {
@@ -405,10 +447,11 @@ int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void*
     const float* rd = h->gather_recv.as<float>();
     const uint32_t* ri = reinterpret_cast<const uint32_t*>(rd + qk);
     KNN_CUDA(knn::launch_merge(rd, ri, static_cast<int64_t>(2 * qk), k, h->n_ranks,
-                               static_cast<int>(k), nq, 0, dst_d, dst_i, out_i64, h->stream));
+                               static_cast<int>(k), nq, 0, dst_d, dst_i, out_i64, h->stream,
+                               overlap));
     launches += 2;
   }
-  if (h->profiling) KNN_CUDA(cudaEventRecord(h->ev[2], h->stream));
+  if (prof) KNN_CUDA(cudaEventRecord((*prof)[2], h->stream));
 
   if (cd == 0)
     KNN_CUDA(cudaMemcpyAsync(distances, dst_d, qk * 4, cudaMemcpyDeviceToHost, h->stream));
@@ -418,17 +461,10 @@ int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void*
   h->kernel_launches += launches;
   h->scan_launches += 1;
 
-  if (!sync && !h->profiling) return KNN_OK;
+  if (!sync) return KNN_OK;
   KNN_CUDA(cudaMemcpyAsync(h->err_host, h->err_dev, sizeof(int), cudaMemcpyDeviceToHost,
                            h->stream));
   if ((st = sync_stream(h)) != KNN_OK) return st;
-  if (h->profiling) {
-    float a = 0.f, b = 0.f;
-    KNN_CUDA(cudaEventElapsedTime(&a, h->ev[0], h->ev[1]));
-    KNN_CUDA(cudaEventElapsedTime(&b, h->ev[1], h->ev[2]));
-    h->scan_ms += a;
-    h->merge_ms += b;
-  }
   return check_device_error(h);
 }
 
@@ -468,7 +504,7 @@ int build_impl(knn_index* h, const void* rows, int dtype, int64_t n, int64_t dim
   KNN_CUDA(cudaMalloc(&h->norms, static_cast<size_t>(n) * 4));
   const size_t esz = dtype == KNN_DTYPE_F16 ? 2 : 4;
   if (where == 1) {
-    KNN_CUDA(knn::launch_convert_rows(rows, dtype == KNN_DTYPE_F16, n, dim, h->data, ld,
+    KNN_CUDA(knn::launch_convert_rows(rows, dtype == KNN_DTYPE_F16, n, n, dim, h->data, ld,
                                       h->norms, h->stream));
     g_dispatch.fetch_add(1);
   } else {
@@ -483,7 +519,7 @@ int build_impl(knn_index* h, const void* rows, int dtype, int64_t n, int64_t dim
       cudaError_t e = cudaMemcpyAsync(stage.ptr, src, static_cast<size_t>(rr) * dim * esz,
                                       cudaMemcpyHostToDevice, h->stream);
       if (e == cudaSuccess)
-        e = knn::launch_convert_rows(stage.ptr, dtype == KNN_DTYPE_F16, rr, dim,
+        e = knn::launch_convert_rows(stage.ptr, dtype == KNN_DTYPE_F16, rr, rr, dim,
                                      h->data + static_cast<size_t>(r0) * ld, ld, h->norms + r0,
                                      h->stream);
       if (e == cudaSuccess) e = cudaStreamSynchronize(h->stream);
@@ -575,6 +611,8 @@ int knn_index_destroy(knn_index* h) {
   if (h->err_host) cudaFreeHost(h->err_host);
   for (auto& ev : h->ev)
     if (ev) cudaEventDestroy(ev);
+  for (auto& t : h->prof_events)
+    for (auto& ev : t) cudaEventDestroy(ev);
   if (h->own_stream) cudaStreamDestroy(h->own_stream);
   delete h;
   return KNN_OK;
@@ -743,6 +781,13 @@ int knn_index_set_profiling(knn_index* h, int enabled) {
 int knn_index_kernel_stats(knn_index* h, double* scan_ms, double* merge_ms,
                            int64_t* scan_launches, int64_t* kernel_launches) {
   if (!h) return fail(KNN_EINVAL, "null index");
+  {
+    std::lock_guard<std::mutex> lock(h->mu);
+    KNN_CUDA(cudaSetDevice(h->device));
+    KNN_CUDA(cudaStreamSynchronize(h->stream));
+    const int st = drain_profile(h);
+    if (st != KNN_OK) return st;
+  }
   if (scan_ms) *scan_ms = h->scan_ms;
   if (merge_ms) *merge_ms = h->merge_ms;
   if (scan_launches) *scan_launches = h->scan_launches;
@@ -752,6 +797,8 @@ int knn_index_kernel_stats(knn_index* h, double* scan_ms, double* merge_ms,
 
 int knn_index_reset_kernel_stats(knn_index* h) {
   if (!h) return fail(KNN_EINVAL, "null index");
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->prof_used = 0;
   h->scan_ms = h->merge_ms = 0.0;
   h->scan_launches = h->kernel_launches = 0;
   return KNN_OK;
@@ -854,7 +901,8 @@ int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
     off += align256(bytes);
     return p;
   };
-  __half* q16 = reinterpret_cast<__half*>(take(static_cast<size_t>(nq) * h->ld * 2));
+  const int64_t nq_pad = knn::padded_query_rows(plan);
+  __half* q16 = reinterpret_cast<__half*>(take(static_cast<size_t>(nq_pad) * h->ld * 2));
   float* qnorm = reinterpret_cast<float*>(take(static_cast<size_t>(nq) * 4));
   float* part_d = reinterpret_cast<float*>(take(static_cast<size_t>(plan.partial_bytes / 2)));
   uint32_t* part_i = reinterpret_cast<uint32_t*>(take(static_cast<size_t>(plan.partial_bytes / 2)));
@@ -873,9 +921,10 @@ int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
                              cudaMemcpyHostToDevice, h->stream));
     qsrc = q32;
   }
-  KNN_CUDA(knn::launch_convert_rows(qsrc, false, nq, h->dim, q16, h->ld, qnorm, h->stream));
+  KNN_CUDA(knn::launch_convert_rows(qsrc, false, nq, nq_pad, h->dim, q16, h->ld, qnorm,
+                                    h->stream));
   CUtensorMap qmap;
-  if ((st = encode_rows(&qmap, q16, nq, h->ld, knn::kQueryRows)) != KNN_OK) return st;
+  if ((st = encode_rows(&qmap, q16, nq_pad, h->ld, knn::kQueryRows)) != KNN_OK) return st;
 
   knn::ScanParams p;
   p.row_norms = h->norms;

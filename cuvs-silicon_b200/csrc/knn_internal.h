@@ -20,7 +20,7 @@ constexpr int kTmemCols = 512;    // double-buffered accumulators
 constexpr int kScanThreads = 192; // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kMaxStages = 8;
 constexpr int kSmemLimit = 232448;        // sm_100 opt-in dynamic smem per CTA
-constexpr int kSmemReserve = 1024 + 256;  // 1 KiB alignment slack + barriers
+constexpr int kSmemReserve = 1024 + 4096 + 512;  // alignment slack + norm staging + barriers
 constexpr int kMaxK = 256;
 constexpr int kRowBuf = 16;       // buffered survivors per query row
 constexpr uint32_t kNoIndex = 0xFFFFFFFFu;
@@ -55,14 +55,25 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
                 Plan* out);
 
 // Launchers (return the CUDA error of the launch).
+// `overlap` launches the kernel as a programmatic dependent of the one
+// before it (its set-up overlaps that kernel's tail); off when the caller
+// brackets kernels with timing events.
 cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
-                        const ScanParams& p, const Plan& plan, cudaStream_t stream);
+                        const ScanParams& p, const Plan& plan, cudaStream_t stream,
+                        bool overlap = true);
 
 // fp32/fp16 rows -> fp16 rows with leading dimension ld (zero padded) plus
 // fp32 norms of the rounded rows.  in_is_half selects the input type.
+// Output rows [rows, rows_out) are written as zeros (no norm).
 cudaError_t launch_convert_rows(const void* in, bool in_is_half, int64_t rows,
-                                int64_t dim, __half* out, int64_t ld, float* norms,
-                                cudaStream_t stream);
+                                int64_t rows_out, int64_t dim, __half* out, int64_t ld,
+                                float* norms, cudaStream_t stream);
+
+// Rows of the fp16 query buffer a search needs: every 128-row query slab
+// the scan kernel loads lies inside it, so no TMA box leaves the buffer.
+inline int64_t padded_query_rows(const Plan& plan) {
+  return (plan.query_tiles - 1) * plan.query_block + kQueryRows;
+}
 
 // Launches the bounded-wait self-test kernel (see knn_scan.cu).
 cudaError_t launch_bounded_wait_selftest(int* err, uint64_t limit_ns, cudaStream_t stream);
@@ -74,6 +85,6 @@ cudaError_t launch_bounded_wait_selftest(int* err, uint64_t limit_ns, cudaStream
 cudaError_t launch_merge(const float* in_d, const uint32_t* in_i, int64_t stride_list,
                          int64_t stride_query, int n_lists, int k, int64_t n_queries,
                          int64_t index_offset, float* out_d, void* out_i, bool out_i64,
-                         cudaStream_t stream);
+                         cudaStream_t stream, bool overlap = true);
 
 }  // namespace knn

@@ -3,17 +3,29 @@
 // The reference selects its final top-k with a serial pass of thread 0 over
 // 128 per-thread lists followed by an insertion sort
 // (shaders/cagra_kernels.metal:636-649).  Here one CTA of 8 warps owns one
-// query: each warp keeps a sorted list of K2 = 32 * E entries in registers
-// (E per lane, element e = r * 32 + lane) and folds in one input list at a
-// time with a bitonic merge:
-//   C[e] = min(A[e], B[K2 - 1 - e])      (the K2 smallest of A u B, bitonic)
+// query and the order is (distance, index), as src/cagra.cpp:229-238;
+// missing entries are (+inf, UINT32_MAX), the padding of
+// src/cagra.cpp:245-250.
+//
+// Threshold path (default).  The input lists are sorted.  With S lists and
+// j = ceil(k / S), let tau be the ceil(k / j)-th smallest of the lists' j-th
+// entries (lexicographic (distance, index)): ceil(k / j) lists then hold j
+// entries each that are <= tau, so the merged k-th entry is <= tau and only
+// entries <= tau can be in the result.  (For k <= S, tau is the k-th
+// smallest list head.)  The CTA finds tau with a small shared-memory sort,
+// filters the entries <= tau into a candidate array and sorts that with one
+// block-wide bitonic sort; typically about k entries pass.
+//
+// Fold path (fallback when more than kCandCap entries pass, e.g. massive
+// exact ties).  Lists are staged in shared memory in batches; each warp
+// keeps a sorted list of K2 = 32 * E entries in registers (element
+// e = r * 32 + lane) and folds lists in with a bitonic merge:
+//   C[e] = min(A[e], B[K2 - 1 - e])   (the K2 smallest of A u B, bitonic)
 //   then log2(K2) compare-exchange stages (register swaps for strides >= 32,
-//   warp shuffles below).
-// A list whose best entry is not better than the running k-th entry is
-// skipped after one compare.  The 8 warp lists are then folded by warp 0
-// through shared memory.  Order is (distance, index), as
-// src/cagra.cpp:229-238; missing entries stay (+inf, UINT32_MAX), the
-// padding of src/cagra.cpp:245-250.
+//   warp shuffles below); the 8 warp lists are folded last by warp 0.
+//
+// The kernel is launched as a programmatic dependent of the kernel before it
+// in the stream and waits (griddepcontrol.wait) before reading its input.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -25,6 +37,10 @@ namespace knn {
 namespace {
 
 constexpr int kMergeWarps = 8;
+constexpr int kStageEntries = 6144;  // 48 KiB of (fp32, uint32) entries (fold path)
+constexpr int kSelCap = 2048;        // lists' j-th entries (threshold path)
+constexpr int kCandCap = 4096;       // threshold-path candidates
+static_assert(kSelCap + kCandCap <= kStageEntries, "threshold arrays share the stage");
 
 __device__ __forceinline__ bool less_pair(float da, uint32_t ia, float db, uint32_t ib) {
   return da < db || (da == db && ia < ib);
@@ -65,7 +81,6 @@ __device__ __forceinline__ void load_list(List<E>& l, const float* d, const uint
 // a <- the K2 smallest of (a, b), sorted ascending; both inputs sorted.
 template <int E>
 __device__ __forceinline__ void merge_into(List<E>& a, const List<E>& b, int lane) {
-  // reverse b and take the element-wise minimum -> bitonic sequence
 #pragma unroll
   for (int r = 0; r < E; ++r) {
     const float bd = __shfl_sync(0xffffffffu, b.d[E - 1 - r], 31 - lane);
@@ -75,7 +90,6 @@ __device__ __forceinline__ void merge_into(List<E>& a, const List<E>& b, int lan
       a.i[r] = bi;
     }
   }
-  // bitonic merge, strides K2/2 ... 32 inside the thread
 #pragma unroll
   for (int rs = E / 2; rs >= 1; rs >>= 1) {
 #pragma unroll
@@ -93,7 +107,6 @@ __device__ __forceinline__ void merge_into(List<E>& a, const List<E>& b, int lan
       }
     }
   }
-  // strides 16 ... 1 across lanes
 #pragma unroll
   for (int s = 16; s >= 1; s >>= 1) {
     const bool upper = (lane & s) != 0;
@@ -128,37 +141,71 @@ __device__ __forceinline__ void get_entry(const List<E>& l, int e, float& d, uin
   i = __shfl_sync(0xffffffffu, iv, e & 31);
 }
 
-template <int E, typename OutIdx>
-__global__ void __launch_bounds__(kMergeWarps * 32)
-    merge_kernel(const float* __restrict__ in_d, const uint32_t* __restrict__ in_i,
-                 int64_t stride_list, int64_t stride_query, int n_lists, int k,
-                 int64_t index_offset, float* __restrict__ out_d, OutIdx* __restrict__ out_i) {
-  extern __shared__ uint8_t smem_raw[];
-  constexpr int K2 = 32 * E;
-  float* sd = reinterpret_cast<float*>(smem_raw);
-  uint32_t* si = reinterpret_cast<uint32_t*>(sd + kMergeWarps * K2);
+template <typename OutIdx>
+__device__ __forceinline__ void store_out(float* out_d, OutIdx* out_i, int64_t at, float d,
+                                          uint32_t idx, int64_t index_offset) {
+  out_d[at] = d;
+  if constexpr (sizeof(OutIdx) == 8) {
+    out_i[at] = idx == kNoIndex ? OutIdx(-1) : static_cast<OutIdx>(idx) + index_offset;
+  } else {
+    out_i[at] = idx == kNoIndex ? kNoIndex : static_cast<uint32_t>(idx + index_offset);
+  }
+}
 
-  const int64_t q = blockIdx.x;
+// Block-wide ascending bitonic sort of p2 (a power of two) entries in
+// shared memory.  All threads of the block call it.
+__device__ __forceinline__ void block_sort(float* d, uint32_t* i, int p2) {
+  for (int size = 2; size <= p2; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int a = threadIdx.x; a < p2 / 2; a += blockDim.x) {
+        const int lo = 2 * a - (a & (stride - 1));
+        const int hi = lo + stride;
+        const bool up = (lo & size) == 0;
+        const float dl = d[lo], dh = d[hi];
+        const uint32_t il = i[lo], ih = i[hi];
+        if (less_pair(dh, ih, dl, il) == up) {
+          d[lo] = dh;
+          i[lo] = ih;
+          d[hi] = dl;
+          i[hi] = il;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Fold path: folds every list of query q; writes the first k entries.
+template <int E, typename OutIdx>
+__device__ void fold_merge(float* sd, uint32_t* si, const float* qd, const uint32_t* qi,
+                           int64_t stride_list, int n_lists, int k, int64_t q,
+                           int64_t index_offset, float* out_d, OutIdx* out_i) {
+  constexpr int K2 = 32 * E;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const float* qd = in_d + q * stride_query;
-  const uint32_t* qi = in_i + q * stride_query;
-
   List<E> acc;
   fill_inf(acc);
-  for (int l = warp; l < n_lists; l += kMergeWarps) {
-    const float* ld = qd + l * stride_list;
-    const uint32_t* li = qi + l * stride_list;
-    // skip lists that cannot improve the current k-th entry
-    float kd;
-    uint32_t ki;
-    get_entry(acc, k - 1, kd, ki);
-    const float b0d = ld[0];
-    const uint32_t b0i = li[0];
-    if (!less_pair(b0d, b0i, kd, ki)) continue;
-    List<E> b;
-    load_list(b, ld, li, k, lane);
-    merge_into(acc, b, lane);
+  const int batch = kStageEntries / k < n_lists ? kStageEntries / k : n_lists;
+  for (int l0 = 0; l0 < n_lists; l0 += batch) {
+    const int nb = n_lists - l0 < batch ? n_lists - l0 : batch;
+    for (int e = threadIdx.x; e < nb * k; e += blockDim.x) {
+      const int l = e / k;
+      const int r = e - l * k;
+      const int64_t at = static_cast<int64_t>(l0 + l) * stride_list + r;
+      sd[e] = qd[at];
+      si[e] = qi[at];
+    }
+    __syncthreads();
+    for (int l = warp; l < nb; l += kMergeWarps) {
+      float kd;
+      uint32_t ki;
+      get_entry(acc, k - 1, kd, ki);
+      if (!less_pair(sd[l * k], si[l * k], kd, ki)) continue;  // cannot improve
+      List<E> b;
+      load_list(b, sd + l * k, si + l * k, k, lane);
+      merge_into(acc, b, lane);
+    }
+    __syncthreads();
   }
   if (warp > 0) {
 #pragma unroll
@@ -181,17 +228,117 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
 #pragma unroll
   for (int r = 0; r < E; ++r) {
     const int e = r * 32 + lane;
-    if (e < k) {
-      const uint32_t idx = acc.i[r];
-      out_d[q * k + e] = acc.d[r];
-      if constexpr (sizeof(OutIdx) == 8) {
-        out_i[q * k + e] = idx == kNoIndex ? OutIdx(-1)
-                                           : static_cast<OutIdx>(idx) + index_offset;
-      } else {
-        out_i[q * k + e] =
-            idx == kNoIndex ? kNoIndex : static_cast<uint32_t>(idx + index_offset);
+    if (e < k) store_out(out_d, out_i, q * k + e, acc.d[r], acc.i[r], index_offset);
+  }
+}
+
+template <int E, typename OutIdx>
+__global__ void __launch_bounds__(kMergeWarps * 32)
+    merge_kernel(const float* __restrict__ in_d, const uint32_t* __restrict__ in_i,
+                 int64_t stride_list, int64_t stride_query, int n_lists, int k,
+                 int64_t index_offset, float* __restrict__ out_d, OutIdx* __restrict__ out_i) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  extern __shared__ uint8_t smem_raw[];
+  float* sd = reinterpret_cast<float*>(smem_raw);
+  uint32_t* si = reinterpret_cast<uint32_t*>(sd + kStageEntries);
+  __shared__ int s_count;
+
+  const int64_t q = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const float* qd = in_d + q * stride_query;
+  const uint32_t* qi = in_i + q * stride_query;
+  const float kInf = __int_as_float(0x7f800000);
+
+  // tau: the r-th smallest of the lists' j-th entries
+  const int j = (k + n_lists - 1) / n_lists;  // >= 1
+  const int r = (k + j - 1) / j;               // <= n_lists
+  float* seld = sd;
+  uint32_t* seli = si;
+  float* cd = sd + kSelCap;
+  uint32_t* ci = si + kSelCap;
+  if (n_lists > kSelCap) {
+    fold_merge<E, OutIdx>(sd, si, qd, qi, stride_list, n_lists, k, q, index_offset, out_d,
+                          out_i);
+    return;
+  }
+  int p2 = 1;
+  while (p2 < n_lists) p2 <<= 1;
+  for (int l = tid; l < p2; l += blockDim.x) {
+    if (l < n_lists) {
+      const int64_t at = static_cast<int64_t>(l) * stride_list + (j - 1);
+      seld[l] = qd[at];
+      seli[l] = qi[at];
+    } else {
+      seld[l] = kInf;
+      seli[l] = kNoIndex;
+    }
+  }
+  if (tid == 0) s_count = 0;
+  __syncthreads();
+  block_sort(seld, seli, p2);
+  const float td = seld[r - 1];
+  const uint32_t ti = seli[r - 1];
+
+  // candidates: every valid entry (d, i) <= tau (every valid entry when
+  // tau is the padding, i.e. when fewer than r lists have j entries)
+  const int total = n_lists * k;
+  constexpr int kPer = 8;  // entries per thread per round, loaded before use
+  for (int e0 = 0; e0 < total; e0 += kPer * kMergeWarps * 32) {
+    float dv[kPer];
+    uint32_t iv[kPer];
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int e = e0 + u * kMergeWarps * 32 + tid;
+      iv[u] = kNoIndex;
+      dv[u] = kInf;
+      if (e < total) {
+        const int l = e / k;
+        const int rr = e - l * k;
+        const int64_t at = static_cast<int64_t>(l) * stride_list + rr;
+        iv[u] = qi[at];
+        dv[u] = qd[at];
       }
     }
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const bool take = iv[u] != kNoIndex && (dv[u] < td || (dv[u] == td && iv[u] <= ti));
+      // warp-aggregated append: one shared atomic per warp
+      const unsigned ballot = __ballot_sync(0xffffffffu, take);
+      if (ballot) {
+        int base = 0;
+        if (lane == 0) base = atomicAdd(&s_count, __popc(ballot));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (take) {
+          const int pos = base + __popc(ballot & ((1u << lane) - 1u));
+          if (pos < kCandCap) {
+            cd[pos] = dv[u];
+            ci[pos] = iv[u];
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const int count = s_count;
+  if (count > kCandCap) {  // block-uniform
+    __syncthreads();
+    fold_merge<E, OutIdx>(sd, si, qd, qi, stride_list, n_lists, k, q, index_offset, out_d,
+                          out_i);
+    return;
+  }
+  int c2 = 1;
+  while (c2 < count) c2 <<= 1;
+  for (int e = count + tid; e < c2; e += blockDim.x) {
+    cd[e] = kInf;
+    ci[e] = kNoIndex;
+  }
+  __syncthreads();
+  block_sort(cd, ci, c2);
+  for (int e = tid; e < k; e += blockDim.x) {
+    const bool have = e < count;
+    store_out(out_d, out_i, q * k + e, have ? cd[e] : kInf, have ? ci[e] : kNoIndex,
+              index_offset);
   }
 }
 
@@ -199,29 +346,44 @@ template <int E>
 cudaError_t launch_e(const float* in_d, const uint32_t* in_i, int64_t stride_list,
                      int64_t stride_query, int n_lists, int k, int64_t n_queries,
                      int64_t index_offset, float* out_d, void* out_i, bool out_i64,
-                     cudaStream_t stream) {
-  const size_t smem = static_cast<size_t>(kMergeWarps) * 32 * E * 8;
-  if (smem > 48 * 1024) {
-    cudaError_t e = out_i64
-                        ? cudaFuncSetAttribute(merge_kernel<E, int64_t>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(smem))
-                        : cudaFuncSetAttribute(merge_kernel<E, uint32_t>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(smem));
+                     cudaStream_t stream, bool overlap) {
+  static_assert(kMergeWarps * 32 * E <= kStageEntries, "warp lists fit the staging area");
+  static_assert(kCandCap <= kStageEntries, "candidates fit the staging area");
+  constexpr size_t smem = static_cast<size_t>(kStageEntries) * 8;
+  // opt in to more than 48 KiB of dynamic shared memory once per device
+  static bool configured[64][2] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const int w = out_i64 ? 1 : 0;
+  if (dev < 0 || dev >= 64 || !configured[dev][w]) {
+    e = out_i64 ? cudaFuncSetAttribute(merge_kernel<E, int64_t>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem))
+                : cudaFuncSetAttribute(merge_kernel<E, uint32_t>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
     if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) configured[dev][w] = true;
   }
-  const unsigned grid = static_cast<unsigned>(n_queries);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(n_queries));
+  cfg.blockDim = dim3(kMergeWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = overlap ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (out_i64) {
-    merge_kernel<E, int64_t><<<grid, kMergeWarps * 32, smem, stream>>>(
-        in_d, in_i, stride_list, stride_query, n_lists, k, index_offset, out_d,
-        static_cast<int64_t*>(out_i));
-  } else {
-    merge_kernel<E, uint32_t><<<grid, kMergeWarps * 32, smem, stream>>>(
-        in_d, in_i, stride_list, stride_query, n_lists, k, index_offset, out_d,
-        static_cast<uint32_t*>(out_i));
+    return cudaLaunchKernelEx(&cfg, merge_kernel<E, int64_t>, in_d, in_i, stride_list,
+                              stride_query, n_lists, k, index_offset, out_d,
+                              static_cast<int64_t*>(out_i));
   }
-  return cudaGetLastError();
+  return cudaLaunchKernelEx(&cfg, merge_kernel<E, uint32_t>, in_d, in_i, stride_list,
+                            stride_query, n_lists, k, index_offset, out_d,
+                            static_cast<uint32_t*>(out_i));
 }
 
 }  // namespace
@@ -229,24 +391,21 @@ cudaError_t launch_e(const float* in_d, const uint32_t* in_i, int64_t stride_lis
 cudaError_t launch_merge(const float* in_d, const uint32_t* in_i, int64_t stride_list,
                          int64_t stride_query, int n_lists, int k, int64_t n_queries,
                          int64_t index_offset, float* out_d, void* out_i, bool out_i64,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, bool overlap) {
   if (n_queries <= 0 || k <= 0) return cudaSuccess;
   if (n_queries > 0x7fffffff) return cudaErrorInvalidValue;
   if (k <= 32)
     return launch_e<1>(in_d, in_i, stride_list, stride_query, n_lists, k, n_queries,
-                       index_offset, out_d, out_i, out_i64, stream);
+                       index_offset, out_d, out_i, out_i64, stream, overlap);
   if (k <= 64)
     return launch_e<2>(in_d, in_i, stride_list, stride_query, n_lists, k, n_queries,
-                       index_offset, out_d, out_i, out_i64, stream);
+                       index_offset, out_d, out_i, out_i64, stream, overlap);
   if (k <= 128)
     return launch_e<4>(in_d, in_i, stride_list, stride_query, n_lists, k, n_queries,
-                       index_offset, out_d, out_i, out_i64, stream);
+                       index_offset, out_d, out_i, out_i64, stream, overlap);
   if (k <= 256)
     return launch_e<8>(in_d, in_i, stride_list, stride_query, n_lists, k, n_queries,
-                       index_offset, out_d, out_i, out_i64, stream);
-  if (k <= 512)
-    return launch_e<16>(in_d, in_i, stride_list, stride_query, n_lists, k, n_queries,
-                        index_offset, out_d, out_i, out_i64, stream);
+                       index_offset, out_d, out_i, out_i64, stream, overlap);
   return cudaErrorInvalidValue;
 }
 

@@ -35,17 +35,20 @@ __device__ __forceinline__ float load_elem(const void* in, int64_t i) {
 // One warp per row, grid-stride over rows.  `vec` selects the 8-wide path:
 // dim % 8 == 0 and the input base 16-byte aligned.
 template <bool kHalfIn>
-__global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, int64_t dim,
-                                    __half* __restrict__ out, int64_t ld,
+__global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, int64_t rows_out,
+                                    int64_t dim, __half* __restrict__ out, int64_t ld,
                                     float* __restrict__ norms, bool vec) {
   const int lane = threadIdx.x & 31;
   const int64_t warps_per_block = blockDim.x >> 5;
   const int64_t first = static_cast<int64_t>(blockIdx.x) * warps_per_block + (threadIdx.x >> 5);
   const int64_t step = static_cast<int64_t>(gridDim.x) * warps_per_block;
-  for (int64_t r = first; r < rows; r += step) {
+  for (int64_t r = first; r < rows_out; r += step) {
     float acc = 0.0f;
     __half* orow = out + r * ld;
-    if (vec) {
+    if (r >= rows) {
+      // padding row: zeros (keeps whole TMA boxes inside the allocation)
+      for (int64_t c = lane; c < ld; c += 32) orow[c] = __float2half_rn(0.0f);
+    } else if (vec) {
       const int64_t groups = dim / 8;
       for (int64_t g = lane; g < groups; g += 32) {
         float v[8];
@@ -94,27 +97,29 @@ __global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, i
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane == 0) norms[r] = acc;
+    if (lane == 0 && r < rows) norms[r] = acc;
   }
 }
 
 }  // namespace
 
-cudaError_t launch_convert_rows(const void* in, bool in_is_half, int64_t rows, int64_t dim,
-                                __half* out, int64_t ld, float* norms, cudaStream_t stream) {
-  if (rows <= 0) return cudaSuccess;
+cudaError_t launch_convert_rows(const void* in, bool in_is_half, int64_t rows, int64_t rows_out,
+                                int64_t dim, __half* out, int64_t ld, float* norms,
+                                cudaStream_t stream) {
+  if (rows_out < rows) rows_out = rows;
+  if (rows_out <= 0) return cudaSuccess;
   const bool vec = (dim % 8 == 0) && ((reinterpret_cast<uintptr_t>(in) & 15u) == 0) &&
                    ((reinterpret_cast<uintptr_t>(out) & 15u) == 0) && (ld % 8 == 0);
   constexpr int kThreads = 256;
-  const int64_t warps_needed = rows;
+  const int64_t warps_needed = rows_out;
   int64_t blocks = (warps_needed + (kThreads / 32) - 1) / (kThreads / 32);
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (in_is_half) {
     convert_rows_kernel<true><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
-        in, rows, dim, out, ld, norms, vec);
+        in, rows, rows_out, dim, out, ld, norms, vec);
   } else {
     convert_rows_kernel<false><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
-        in, rows, dim, out, ld, norms, vec);
+        in, rows, rows_out, dim, out, ld, norms, vec);
   }
   return cudaGetLastError();
 }

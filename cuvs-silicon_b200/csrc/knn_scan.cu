@@ -81,6 +81,7 @@ struct Smem {
   uint32_t* heap_i;
   float* buf_d;
   uint32_t* buf_i;
+  float* norm_stage;  // [4 epilogue warps][kAccCols] row norms of the current tile
   uint64_t* full;
   uint64_t* empty;
   uint64_t* acc_full;
@@ -98,7 +99,8 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, const ScanParams& p) {
   s.heap_i = reinterpret_cast<uint32_t*>(s.heap_d + static_cast<size_t>(p.k) * p.query_block);
   s.buf_d = reinterpret_cast<float*>(s.heap_i + static_cast<size_t>(p.k) * p.query_block);
   s.buf_i = reinterpret_cast<uint32_t*>(s.buf_d + static_cast<size_t>(kRowBuf) * p.query_block);
-  uintptr_t b = reinterpret_cast<uintptr_t>(s.buf_i + static_cast<size_t>(kRowBuf) * p.query_block);
+  s.norm_stage = reinterpret_cast<float*>(s.buf_i + static_cast<size_t>(kRowBuf) * p.query_block);
+  uintptr_t b = reinterpret_cast<uintptr_t>(s.norm_stage + 4 * kAccCols);
   b = (b + 7) & ~static_cast<uintptr_t>(7);
   uint64_t* bars = reinterpret_cast<uint64_t*>(b);
   s.full = bars;
@@ -310,6 +312,19 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
     st.rd = kInf;
     st.ri = kNoIndex;
     st.cnt = 0;
+    // Row norms are prefetched one tile ahead into registers, then staged in
+    // this warp's slice of shared memory so the chunk loop reads them with
+    // a shared-memory load instead of waiting on DRAM once per chunk.
+    float* const ns = sm.norm_stage + (warp - 2) * kAccCols;
+    float nx[kAccCols / 32];
+    auto prefetch_norms = [&](int64_t tile) {
+#pragma unroll
+      for (int c = 0; c < kAccCols / 32; ++c) {
+        const int64_t col = tile * kTileRows + c * 32 + lane;
+        nx[c] = col < p.n_rows ? __ldg(p.row_norms + col) : kInf;
+      }
+    };
+    if (warp_active) prefetch_norms(t0);
     for (int64_t t = t0; t < t1; ++t) {
       const uint32_t b = tc & 1u;
       // every lane waits; the warp leaves together if any lane gave up, so
@@ -321,6 +336,10 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
       }
       tc_fence_after();
       if (warp_active) {
+#pragma unroll
+        for (int c = 0; c < kAccCols / 32; ++c) ns[c * 32 + lane] = nx[c];
+        __syncwarp();
+        if (t + 1 < t1) prefetch_norms(t + 1);
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + b * kAccCols;
         if (t == t0 && k <= 32) {
           float g[32];
@@ -328,14 +347,18 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
           for (int j = 0; j < 32; ++j) g[j] = kInf;
 #pragma unroll 1
           for (int c = 0; c < kAccCols / 32; ++c) {
-            const int64_t col = t * kTileRows + c * 32 + lane;
-            const float xn = col < p.n_rows ? __ldg(p.row_norms + col) : kInf;
             uint32_t r[32];
             tmem_ld_32x32b_x32(tbase + c * 32, r);
-            tmem_ld_wait();
+            tmem_ld_wait_into(r);
+            const float4* n4 = reinterpret_cast<const float4*>(ns + c * 32);
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              g[j] = fminf(g[j], l2_from_dot(r[j], qn, __shfl_sync(0xffffffffu, xn, j)));
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const float4 v = n4[j4];  // same address in every lane: broadcast
+              g[4 * j4 + 0] = fminf(g[4 * j4 + 0], l2_from_dot(r[4 * j4 + 0], qn, v.x));
+              g[4 * j4 + 1] = fminf(g[4 * j4 + 1], l2_from_dot(r[4 * j4 + 1], qn, v.y));
+              g[4 * j4 + 2] = fminf(g[4 * j4 + 2], l2_from_dot(r[4 * j4 + 2], qn, v.z));
+              g[4 * j4 + 3] = fminf(g[4 * j4 + 3], l2_from_dot(r[4 * j4 + 3], qn, v.w));
+            }
           }
           sort32(g);
           // g is ascending, so g[k - 1] = max of g[0..k-1] (written without a
@@ -346,17 +369,18 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
           // keep d <= tk: the next float up (tk >= 0 here)
           if (valid_q && tk < kInf) st.thr = fminf(st.thr, __int_as_float(__float_as_int(tk) + 1));
         }
-#pragma unroll 1
-        for (int c = 0; c < kAccCols / 32; ++c) {
-          // row norm of column (c * 32 + lane); its load overlaps the TMEM load
-          const int64_t col = t * kTileRows + c * 32 + lane;
-          const float xn = col < p.n_rows ? __ldg(p.row_norms + col) : kInf;
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tbase + c * 32, r);
-          tmem_ld_wait();
+        // One 32-column chunk: distances, threshold filter, survivor buffer.
+        auto process_chunk = [&](const uint32_t (&r)[32], int c) {
           float dv[32];
+          const float4* n4 = reinterpret_cast<const float4*>(ns + c * 32);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) dv[j] = l2_from_dot(r[j], qn, __shfl_sync(0xffffffffu, xn, j));
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 v = n4[j4];  // row norms of columns 4*j4.., broadcast
+            dv[4 * j4 + 0] = l2_from_dot(r[4 * j4 + 0], qn, v.x);
+            dv[4 * j4 + 1] = l2_from_dot(r[4 * j4 + 1], qn, v.y);
+            dv[4 * j4 + 2] = l2_from_dot(r[4 * j4 + 2], qn, v.z);
+            dv[4 * j4 + 3] = l2_from_dot(r[4 * j4 + 3], qn, v.w);
+          }
           const uint32_t col0 = static_cast<uint32_t>(t * kTileRows + c * 32);
 #pragma unroll
           for (int h = 0; h < 32; h += kRowBuf) {
@@ -380,12 +404,30 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
               }
             }
           }
+        };
+        // TMEM loads double-buffered: chunk c + 1 is in flight while chunk c
+        // is processed.
+        static_assert((kAccCols / 32) % 2 == 0, "chunk pairs");
+        uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32(tbase, ra);
+        tmem_ld_wait_into(ra);
+#pragma unroll 1
+        for (int c = 0; c < kAccCols / 32; c += 2) {
+          tmem_ld_32x32b_x32(tbase + (c + 1) * 32, rb);
+          process_chunk(ra, c);
+          tmem_ld_wait_into(rb);
+          if (c + 2 < kAccCols / 32) tmem_ld_32x32b_x32(tbase + (c + 2) * 32, ra);
+          process_chunk(rb, c + 1);
+          if (c + 2 < kAccCols / 32) tmem_ld_wait_into(ra);
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
       ++tc;
+      // survivors enter the heap at every tile end so thr tightens early (the
+      // accumulator is already released; this overlaps the next tile's MMAs)
+      if (warp_active && __any_sync(0xffffffffu, st.cnt > 0)) flush_buffer(st, sm, k, stride, row);
     }
     if (failed) break;
     if (warp_active) flush_buffer(st, sm, k, stride, row);
@@ -443,6 +485,11 @@ __global__ void __launch_bounds__(kScanThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *sm.tmem_slot;
+  // Launched as a programmatic dependent: the set-up above overlaps the tail
+  // of the kernel before (the query conversion); wait for its results here,
+  // and let the merge kernel after this one be scheduled early.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     if (lane == 0) producer(&qmap, &xmap, p, sm);
@@ -535,7 +582,7 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
 }
 
 cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap, const ScanParams& p,
-                        const Plan& plan, cudaStream_t stream) {
+                        const Plan& plan, cudaStream_t stream, bool overlap) {
   // the opt-in shared-memory limit is a per-device function attribute
   static bool configured[64] = {};
   int dev = 0;
@@ -547,9 +594,17 @@ cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap, const 
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  knn_scan_kernel<<<static_cast<unsigned>(plan.grid), kScanThreads,
-                    static_cast<size_t>(plan.smem_bytes), stream>>>(qmap, xmap, p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(plan.grid));
+  cfg.blockDim = dim3(kScanThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(plan.smem_bytes);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = overlap ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, knn_scan_kernel, qmap, xmap, p);
 }
 
 }  // namespace knn
