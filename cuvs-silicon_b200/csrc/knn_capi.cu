@@ -244,12 +244,20 @@ int poll_nccl(knn_index* h, double seconds) {
       h->comm = nullptr;
       return fail(KNN_ENCCL, "NCCL async error: %s", nccl_str(st));
     }
-    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > seconds) {
+    const double waited =
+        std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (waited > seconds) {
       nccl().CommAbort(h->comm);
       h->comm = nullptr;
       return fail(KNN_ENCCL, "NCCL operation did not complete within %.0f s", seconds);
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
+    // spin for the first millisecond (enqueueing normally takes microseconds),
+    // then back off
+    if (waited < 1e-3) {
+      std::this_thread::yield();
+    } else {
+      std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
   }
 }
 

@@ -43,44 +43,45 @@ namespace knn {
 
 namespace {
 
-__device__ __forceinline__ bool worse(float da, uint32_t ia, float db, uint32_t ib) {
-  return da > db || (da == db && ia > ib);
+// A (distance, index) pair as one 64-bit key: distance bits above, index
+// below.  Distances here are >= 0 (clamped) or +inf, whose IEEE bit
+// patterns order like the values, so comparing keys as unsigned integers is
+// exactly the (distance, index) lexicographic order of src/cagra.cpp:233-238.
+__device__ __forceinline__ uint64_t make_key(float d, uint32_t i) {
+  return (static_cast<uint64_t>(__float_as_uint(d)) << 32) | i;
 }
+__device__ __forceinline__ float key_dist(uint64_t key) {
+  return __uint_as_float(static_cast<uint32_t>(key >> 32));
+}
+constexpr uint64_t kEmptyKey = (static_cast<uint64_t>(0x7f800000u) << 32) | 0xFFFFFFFFull;
 
-// Max-heap of (distance, index) stored column-wise: entry `pos` of query row
-// `row` lives at [pos * stride + row], so the 32 threads of a warp always hit
-// 32 distinct banks whatever positions they touch.
-__device__ __forceinline__ void heap_sift_down(float* hd, uint32_t* hi, int size, int stride,
-                                               int row, int pos, float d, uint32_t i) {
+// Max-heap of keys stored column-wise: entry `pos` of query row `row` lives
+// at [pos * stride + row], so the 32 threads of a warp always touch 32
+// consecutive 8-byte words whatever positions they visit.
+__device__ __forceinline__ void heap_sift_down(uint64_t* h, int size, int stride, int row, int pos,
+                                               uint64_t key) {
   while (true) {
     int c = 2 * pos + 1;
     if (c >= size) break;
-    float cd = hd[c * stride + row];
-    uint32_t ci = hi[c * stride + row];
+    uint64_t ck = h[c * stride + row];
     if (c + 1 < size) {
-      const float rd = hd[(c + 1) * stride + row];
-      const uint32_t ri = hi[(c + 1) * stride + row];
-      if (worse(rd, ri, cd, ci)) {
+      const uint64_t rk = h[(c + 1) * stride + row];
+      if (rk > ck) {
         c += 1;
-        cd = rd;
-        ci = ri;
+        ck = rk;
       }
     }
-    if (!worse(cd, ci, d, i)) break;
-    hd[pos * stride + row] = cd;
-    hi[pos * stride + row] = ci;
+    if (ck <= key) break;
+    h[pos * stride + row] = ck;
     pos = c;
   }
-  hd[pos * stride + row] = d;
-  hi[pos * stride + row] = i;
+  h[pos * stride + row] = key;
 }
 
 struct Smem {
   uint8_t* stages;
-  float* heap_d;
-  uint32_t* heap_i;
-  float* buf_d;
-  uint32_t* buf_i;
+  uint64_t* heap;  // [k][query_block] keys
+  uint64_t* buf;   // [kRowBuf][query_block] buffered survivor keys
   float* norm_stage;  // [4 epilogue warps][kAccCols] row norms of the current tile
   uint64_t* full;
   uint64_t* empty;
@@ -95,11 +96,9 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, const ScanParams& p) {
   const uint32_t base = smem_addr(raw);
   const uint32_t pad = (1024u - (base & 1023u)) & 1023u;
   s.stages = raw + pad;
-  s.heap_d = reinterpret_cast<float*>(s.stages + static_cast<size_t>(p.stages) * kStageBytes);
-  s.heap_i = reinterpret_cast<uint32_t*>(s.heap_d + static_cast<size_t>(p.k) * p.query_block);
-  s.buf_d = reinterpret_cast<float*>(s.heap_i + static_cast<size_t>(p.k) * p.query_block);
-  s.buf_i = reinterpret_cast<uint32_t*>(s.buf_d + static_cast<size_t>(kRowBuf) * p.query_block);
-  s.norm_stage = reinterpret_cast<float*>(s.buf_i + static_cast<size_t>(kRowBuf) * p.query_block);
+  s.heap = reinterpret_cast<uint64_t*>(s.stages + static_cast<size_t>(p.stages) * kStageBytes);
+  s.buf = s.heap + static_cast<size_t>(p.k) * p.query_block;
+  s.norm_stage = reinterpret_cast<float*>(s.buf + static_cast<size_t>(kRowBuf) * p.query_block);
   uintptr_t b = reinterpret_cast<uintptr_t>(s.norm_stage + 4 * kAccCols);
   b = (b + 7) & ~static_cast<uintptr_t>(7);
   uint64_t* bars = reinterpret_cast<uint64_t*>(b);
@@ -213,7 +212,7 @@ __device__ void mma_issuer(const ScanParams& p, const Smem& sm, uint32_t tmem_ba
 // Used by every pass over a tile so all passes see identical values.
 __device__ __forceinline__ float l2_from_dot(uint32_t acc_bits, float qn, float xn) {
   const float d = fmaf(-2.0f, __uint_as_float(acc_bits), qn + xn);
-  return d < 0.0f ? 0.0f : d;
+  return d <= 0.0f ? 0.0f : d;  // also maps -0 to +0 (key order); NaN stays NaN
 }
 
 // Ascending sort of 32 registers: bitonic network with every index a
@@ -244,10 +243,9 @@ __device__ __forceinline__ void sort32(float (&g)[32]) { bitonic_sort<2>(g); }
 // Per query row (one epilogue lane): the filter threshold, the heap root
 // and the number of buffered survivors.
 struct RowState {
-  float thr;   // candidates with d < thr are kept
-  float rd;    // heap root (worst kept) distance and index
-  uint32_t ri;
-  int cnt;     // survivors waiting in the row's buffer
+  float thr;     // candidates with d < thr are kept
+  uint64_t root; // heap root key (worst kept entry)
+  int cnt;       // survivors waiting in the row's buffer
 };
 
 // Moves every lane's buffered survivors into its heap.  Warp-uniform: all
@@ -258,17 +256,15 @@ __device__ __forceinline__ void flush_buffer(RowState& st, const Smem& sm, int k
   const int maxc = __reduce_max_sync(0xffffffffu, st.cnt);
   for (int b = 0; b < maxc; ++b) {
     if (b < st.cnt) {
-      const float d = sm.buf_d[b * stride + row];
-      const uint32_t i = sm.buf_i[b * stride + row];
-      if (d < st.rd || (d == st.rd && i < st.ri)) {
-        heap_sift_down(sm.heap_d, sm.heap_i, k, stride, row, 0, d, i);
-        st.rd = sm.heap_d[row];
-        st.ri = sm.heap_i[row];
+      const uint64_t key = sm.buf[b * stride + row];
+      if (key < st.root) {
+        heap_sift_down(sm.heap, k, stride, row, 0, key);
+        st.root = sm.heap[row];
       }
     }
   }
   st.cnt = 0;
-  st.thr = fminf(st.thr, st.rd);
+  st.thr = fminf(st.thr, key_dist(st.root));
 }
 
 // Epilogue warp.  Lane `row` owns query row `row` of the unit's query block.
@@ -302,15 +298,11 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
     const bool valid_q = warp_active && row < p.query_block && q < p.n_queries;
     const float qn = valid_q ? p.query_norms[q] : 0.0f;
     if (valid_q) {
-      for (int pos = 0; pos < k; ++pos) {
-        sm.heap_d[pos * stride + row] = kInf;
-        sm.heap_i[pos * stride + row] = kNoIndex;
-      }
+      for (int pos = 0; pos < k; ++pos) sm.heap[pos * stride + row] = kEmptyKey;
     }
     RowState st;
     st.thr = valid_q ? kInf : __int_as_float(0xff800000);
-    st.rd = kInf;
-    st.ri = kNoIndex;
+    st.root = kEmptyKey;
     st.cnt = 0;
     // Row norms are prefetched one tile ahead into registers, then staged in
     // this warp's slice of shared memory so the chunk loop reads them with
@@ -397,8 +389,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
 #pragma unroll
               for (int j = 0; j < kRowBuf; ++j) {
                 if ((mask >> j) & 1u) {
-                  sm.buf_d[st.cnt * stride + row] = dv[h + j];
-                  sm.buf_i[st.cnt * stride + row] = col0 + h + j;
+                  sm.buf[st.cnt * stride + row] = make_key(dv[h + j], col0 + h + j);
                   ++st.cnt;
                 }
               }
@@ -434,20 +425,18 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
     if (valid_q) {
       // heap sort -> ascending (distance, index)
       for (int end = k - 1; end > 0; --end) {
-        const float rd = sm.heap_d[row];
-        const uint32_t ri = sm.heap_i[row];
-        const float ed = sm.heap_d[end * stride + row];
-        const uint32_t ei = sm.heap_i[end * stride + row];
-        sm.heap_d[end * stride + row] = rd;
-        sm.heap_i[end * stride + row] = ri;
-        heap_sift_down(sm.heap_d, sm.heap_i, end, stride, row, 0, ed, ei);
+        const uint64_t top = sm.heap[row];
+        const uint64_t last = sm.heap[end * stride + row];
+        sm.heap[end * stride + row] = top;
+        heap_sift_down(sm.heap, end, stride, row, 0, last);
       }
       const int s = u / p.query_tiles;
       float* od = p.part_d + (static_cast<size_t>(q) * p.splits + s) * k;
       uint32_t* oi = p.part_i + (static_cast<size_t>(q) * p.splits + s) * k;
       for (int r = 0; r < k; ++r) {
-        od[r] = sm.heap_d[r * stride + row];
-        oi[r] = sm.heap_i[r * stride + row];
+        const uint64_t key = sm.heap[r * stride + row];
+        od[r] = key_dist(key);
+        oi[r] = static_cast<uint32_t>(key);
       }
     }
   }
