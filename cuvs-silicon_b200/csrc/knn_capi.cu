@@ -68,8 +68,10 @@ int fail(int status, const char* fmt, ...) {
 struct DevBuf {
   void* ptr = nullptr;
   size_t bytes = 0;
+  bool grew = false;  // set when ensure() reallocated (pointers changed)
   int ensure(size_t need) {
     if (need <= bytes) return KNN_OK;
+    grew = true;
     if (ptr) cudaFree(ptr);
     ptr = nullptr;
     bytes = 0;
@@ -220,6 +222,25 @@ struct knn_index {
   ncclComm_t comm = nullptr;
   int n_ranks = 1, rank = 0;
 
+  // CUDA graphs of the device-side search pipeline, replayed when a search
+  // repeats the buffers and shape of a captured one.  `generation` changes
+  // whenever a pointer a graph captured may have changed (scratch growth,
+  // rebuild, stream or communicator change) and invalidates every graph.
+  struct GraphEntry {
+    const void* queries;
+    const void* neighbors;
+    const void* distances;
+    int64_t nq, k;
+    bool i64;
+    cudaStream_t stream;
+    uint64_t generation;
+    int launches;
+    cudaGraphExec_t exec;
+  };
+  bool use_graphs = true;
+  uint64_t generation = 1;
+  std::vector<GraphEntry> graphs;
+
   // profiling: one (before scan, after scan, after merge) event triple per
   // search, read back when the stats are requested
   bool profiling = false;
@@ -289,6 +310,12 @@ int sync_stream(knn_index* h) {
   }
 }
 
+void drop_graphs(knn_index* h) {
+  for (auto& g : h->graphs)
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+  h->graphs.clear();
+}
+
 // Adds the durations of the recorded event triples (the stream must be idle).
 int drain_profile(knn_index* h) {
   for (size_t i = 0; i < h->prof_used; ++i) {
@@ -345,44 +372,17 @@ int validate_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
   return KNN_OK;
 }
 
-// Core search.  out_i64: neighbours are int64.  sync: block and check.
-int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void* neighbors,
-                float* distances, bool out_i64, bool sync, bool require_device) {
-  int st = validate_search(h, queries, nq, k, neighbors, distances);
-  if (st != KNN_OK || nq == 0 || k == 0) return st;
-  std::lock_guard<std::mutex> lock(h->mu);
-  KNN_CUDA(cudaSetDevice(h->device));
-
-  const int cq = classify(queries, h->device);
-  const int cn = classify(neighbors, h->device);
-  const int cd = classify(distances, h->device);
-  if (cq < 0 || cn < 0 || cd < 0)
-    return fail(KNN_EINVAL, "buffer lives on a different device than the index");
-  if (require_device && (cq == 0 || cn == 0 || cd == 0))
-    return fail(KNN_EINVAL, "knn_index_search_async requires device buffers");
-
-  Plan plan;
-  const int pst = knn::plan_search(h->n, h->dim, nq, k, h->num_sms, &plan);
-  if (pst != 0) return fail(pst, "k = %lld is outside the engine's limits", (long long)k);
-
-  // scratch
+// Everything a search enqueues on the device between the query upload and
+// the result download: query conversion, scan, merge(s) and the all-gather.
+// Captured into a CUDA graph when the search is replayable.
+int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, const Plan& plan,
+                     float* dst_d, void* dst_i, bool out_i64,
+                     std::array<cudaEvent_t, 3>* prof, int* launches_out) {
+  int st;
   const size_t qk = static_cast<size_t>(nq) * k;
   const int64_t nq_pad = knn::padded_query_rows(plan);
-  if ((st = h->q16.ensure(static_cast<size_t>(nq_pad) * h->ld * 2)) != KNN_OK) return st;
-  if ((st = h->qnorm.ensure(static_cast<size_t>(nq) * 4)) != KNN_OK) return st;
-  if ((st = h->part_d.ensure(static_cast<size_t>(plan.partial_bytes / 2))) != KNN_OK) return st;
-  if ((st = h->part_i.ensure(static_cast<size_t>(plan.partial_bytes / 2))) != KNN_OK) return st;
-
-  const float* qsrc = queries;
-  if (cq == 0) {
-    if ((st = h->q32.ensure(static_cast<size_t>(nq) * h->dim * 4)) != KNN_OK) return st;
-    KNN_CUDA(cudaMemcpyAsync(h->q32.ptr, queries, static_cast<size_t>(nq) * h->dim * 4,
-                             cudaMemcpyHostToDevice, h->stream));
-    qsrc = h->q32.as<float>();
-  }
   KNN_CUDA(knn::launch_convert_rows(qsrc, false, nq, nq_pad, h->dim, h->q16.as<__half>(),
                                     h->ld, h->qnorm.as<float>(), h->stream));
-
   CUtensorMap qmap;
   if ((st = encode_rows(&qmap, h->q16.as<__half>(), nq_pad, h->ld, knn::kQueryRows)) != KNN_OK)
     return st;
@@ -405,28 +405,11 @@ int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void*
   p.stages = static_cast<int32_t>(plan.stages);
   p.dataset_evict_first = plan.query_tiles == 1 ? 1 : 0;
 
-  std::array<cudaEvent_t, 3>* prof = nullptr;
-  if (h->profiling) {
-    if ((st = next_profile_slot(h, &prof)) != KNN_OK) return st;
-    KNN_CUDA(cudaEventRecord((*prof)[0], h->stream));
-  }
+  if (prof) KNN_CUDA(cudaEventRecord((*prof)[0], h->stream));
   // with timing events between kernels, launch them plainly serialised
   const bool overlap = prof == nullptr;
   KNN_CUDA(knn::launch_scan(qmap, h->xmap, p, plan, h->stream, overlap));
   if (prof) KNN_CUDA(cudaEventRecord((*prof)[1], h->stream));
-
-  // destination of the merged result
-  const size_t idx_bytes = qk * (out_i64 ? 8 : 4);
-  float* dst_d = distances;
-  void* dst_i = neighbors;
-  if (cd == 0) {
-    if ((st = h->out_d.ensure(qk * 4)) != KNN_OK) return st;
-    dst_d = h->out_d.as<float>();
-  }
-  if (cn == 0) {
-    if ((st = h->out_i.ensure(idx_bytes)) != KNN_OK) return st;
-    dst_i = h->out_i.ptr;
-  }
 
   int launches = 2;
   if (!h->comm) {
@@ -437,15 +420,13 @@ int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void*
   } else {
     // local merge into the send buffer: [dist k floats | idx k uint32] per query
     const size_t list_bytes = qk * 8;
-    if ((st = h->gather_send.ensure(list_bytes)) != KNN_OK) return st;
-    if ((st = h->gather_recv.ensure(list_bytes * h->n_ranks)) != KNN_OK) return st;
     float* send_d = h->gather_send.as<float>();
     uint32_t* send_i = reinterpret_cast<uint32_t*>(send_d + qk);
     KNN_CUDA(knn::launch_merge(p.part_d, p.part_i, k, plan.splits * k,
                                static_cast<int>(plan.splits), static_cast<int>(k), nq,
                                h->row_offset, send_d, send_i, false, h->stream, overlap));
     ncclResult_t r = nccl().AllGather(h->gather_send.ptr, h->gather_recv.ptr, list_bytes,
-                                   ncclUint8, h->comm, h->stream);
+                                      ncclUint8, h->comm, h->stream);
     if (r == ncclInProgress) {
       if ((st = poll_nccl(h, 60.0)) != KNN_OK) return st;
     } else if (r != ncclSuccess) {
@@ -460,6 +441,134 @@ int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void*
     launches += 2;
   }
   if (prof) KNN_CUDA(cudaEventRecord((*prof)[2], h->stream));
+  *launches_out = launches;
+  return KNN_OK;
+}
+
+// Core search.  out_i64: neighbours are int64.  sync: block and check.
+int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void* neighbors,
+                float* distances, bool out_i64, bool sync, bool require_device) {
+  int st = validate_search(h, queries, nq, k, neighbors, distances);
+  if (st != KNN_OK || nq == 0 || k == 0) return st;
+  std::lock_guard<std::mutex> lock(h->mu);
+  KNN_CUDA(cudaSetDevice(h->device));
+
+  const int cq = classify(queries, h->device);
+  const int cn = classify(neighbors, h->device);
+  const int cd = classify(distances, h->device);
+  if (cq < 0 || cn < 0 || cd < 0)
+    return fail(KNN_EINVAL, "buffer lives on a different device than the index");
+  if (require_device && (cq == 0 || cn == 0 || cd == 0))
+    return fail(KNN_EINVAL, "knn_index_search_async requires device buffers");
+
+  Plan plan;
+  const int pst = knn::plan_search(h->n, h->dim, nq, k, h->num_sms, &plan);
+  if (pst != 0) return fail(pst, "k = %lld is outside the engine's limits", (long long)k);
+
+  // scratch: everything is sized before any work is enqueued or captured
+  const size_t qk = static_cast<size_t>(nq) * k;
+  const size_t idx_bytes = qk * (out_i64 ? 8 : 4);
+  const int64_t nq_pad = knn::padded_query_rows(plan);
+  DevBuf* bufs[] = {&h->q16, &h->qnorm, &h->part_d, &h->part_i, &h->q32,
+                    &h->out_d, &h->out_i, &h->gather_send, &h->gather_recv};
+  for (DevBuf* b : bufs) b->grew = false;
+  if ((st = h->q16.ensure(static_cast<size_t>(nq_pad) * h->ld * 2)) != KNN_OK) return st;
+  if ((st = h->qnorm.ensure(static_cast<size_t>(nq) * 4)) != KNN_OK) return st;
+  if ((st = h->part_d.ensure(static_cast<size_t>(plan.partial_bytes / 2))) != KNN_OK) return st;
+  if ((st = h->part_i.ensure(static_cast<size_t>(plan.partial_bytes / 2))) != KNN_OK) return st;
+  if (cq == 0 && (st = h->q32.ensure(static_cast<size_t>(nq) * h->dim * 4)) != KNN_OK) return st;
+  if (cd == 0 && (st = h->out_d.ensure(qk * 4)) != KNN_OK) return st;
+  if (cn == 0 && (st = h->out_i.ensure(idx_bytes)) != KNN_OK) return st;
+  if (h->comm) {
+    if ((st = h->gather_send.ensure(qk * 8)) != KNN_OK) return st;
+    if ((st = h->gather_recv.ensure(qk * 8 * h->n_ranks)) != KNN_OK) return st;
+  }
+  for (DevBuf* b : bufs) {
+    if (b->grew) {
+      ++h->generation;
+      drop_graphs(h);
+      break;
+    }
+  }
+
+  const float* qsrc = queries;
+  if (cq == 0) {
+    KNN_CUDA(cudaMemcpyAsync(h->q32.ptr, queries, static_cast<size_t>(nq) * h->dim * 4,
+                             cudaMemcpyHostToDevice, h->stream));
+    qsrc = h->q32.as<float>();
+  }
+  float* dst_d = cd == 0 ? h->out_d.as<float>() : distances;
+  void* dst_i = cn == 0 ? h->out_i.ptr : neighbors;
+
+  int launches = 0;
+  std::array<cudaEvent_t, 3>* prof = nullptr;
+  if (h->profiling) {
+    if ((st = next_profile_slot(h, &prof)) != KNN_OK) return st;
+  }
+  // Replay a graph for device-resident searches that repeat buffers + shape.
+  const bool graphable = h->use_graphs && !prof && cq == 1 && cn == 1 && cd == 1;
+  knn_index::GraphEntry* hit = nullptr;
+  if (graphable) {
+    for (auto& g : h->graphs) {
+      if (g.queries == queries && g.neighbors == neighbors && g.distances == distances &&
+          g.nq == nq && g.k == k && g.i64 == out_i64 && g.stream == h->stream &&
+          g.generation == h->generation) {
+        hit = &g;
+        break;
+      }
+    }
+    if (hit && hit->exec == nullptr) {
+      // second search with this key: capture it now (the first ran directly,
+      // which also performed the one-time per-device kernel set-up)
+      h->graphs.erase(h->graphs.begin() + (hit - h->graphs.data()));
+      hit = nullptr;
+    } else if (!hit) {
+      if (h->graphs.size() >= 8) {
+        if (h->graphs.front().exec) cudaGraphExecDestroy(h->graphs.front().exec);
+        h->graphs.erase(h->graphs.begin());
+      }
+      h->graphs.push_back({queries, neighbors, distances, nq, k, out_i64, h->stream,
+                           h->generation, 0, nullptr});
+      goto direct;
+    }
+    if (!hit) {
+      cudaGraph_t graph = nullptr;
+      cudaGraphExec_t exec = nullptr;
+      bool ok = cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal) ==
+                cudaSuccess;
+      int cst = KNN_OK;
+      if (ok) {
+        cst = enqueue_pipeline(h, qsrc, nq, k, plan, dst_d, dst_i, out_i64, nullptr, &launches);
+        ok = cudaStreamEndCapture(h->stream, &graph) == cudaSuccess && cst == KNN_OK;
+      }
+      if (ok) ok = cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
+      if (graph) cudaGraphDestroy(graph);
+      cudaGetLastError();
+      if (ok) {
+        if (h->graphs.size() >= 8) {
+          if (h->graphs.front().exec) cudaGraphExecDestroy(h->graphs.front().exec);
+          h->graphs.erase(h->graphs.begin());
+        }
+        h->graphs.push_back({queries, neighbors, distances, nq, k, out_i64, h->stream,
+                             h->generation, launches, exec});
+        hit = &h->graphs.back();
+      } else {
+        // capture is not available here: run searches directly from now on
+        if (exec) cudaGraphExecDestroy(exec);
+        h->use_graphs = false;
+        if (cst != KNN_OK) return cst;
+      }
+    }
+  }
+direct:
+  if (hit) {
+    KNN_CUDA(cudaGraphLaunch(hit->exec, h->stream));
+    launches = hit->launches;
+  } else {
+    if ((st = enqueue_pipeline(h, qsrc, nq, k, plan, dst_d, dst_i, out_i64, prof,
+                               &launches)) != KNN_OK)
+      return st;
+  }
 
   if (cd == 0)
     KNN_CUDA(cudaMemcpyAsync(distances, dst_d, qk * 4, cudaMemcpyDeviceToHost, h->stream));
@@ -542,6 +651,8 @@ int build_impl(knn_index* h, const void* rows, int dtype, int64_t n, int64_t dim
   KNN_CUDA(cudaStreamSynchronize(h->stream));
   int st = encode_rows(&h->xmap, h->data, n, ld, knn::kTileRows);
   if (st != KNN_OK) return st;
+  ++h->generation;
+  drop_graphs(h);
   h->n = n;
   h->dim = dim;
   h->ld = ld;
@@ -609,6 +720,7 @@ int knn_index_destroy(knn_index* h) {
   if (!h) return KNN_OK;
   cudaSetDevice(h->device);
   if (h->stream) cudaStreamSynchronize(h->stream);
+  drop_graphs(h);
   if (h->comm) nccl().CommDestroy(h->comm);
   for (DevBuf* b : {&h->q32, &h->q16, &h->qnorm, &h->part_d, &h->part_i, &h->out_d, &h->out_i,
                     &h->gather_send, &h->gather_recv})
@@ -630,7 +742,7 @@ int knn_index_set_stream(knn_index* h, void* stream) {
   if (!h) return fail(KNN_EINVAL, "null index");
   std::lock_guard<std::mutex> lock(h->mu);
   h->stream = stream ? static_cast<cudaStream_t>(stream) : h->own_stream;
-  return KNN_OK;
+  return KNN_OK;  // graphs are keyed on the stream
 }
 
 int knn_index_build(knn_index* h, const void* rows, int dtype, int64_t n, int64_t dim,
@@ -758,6 +870,8 @@ int knn_index_attach_comm(knn_index* h, const void* uid, int n_ranks, int rank) 
     nccl().CommDestroy(h->comm);
     h->comm = nullptr;
   }
+  ++h->generation;
+  drop_graphs(h);
   if (n_ranks == 1) {
     h->n_ranks = 1;
     h->rank = 0;
@@ -777,6 +891,15 @@ int knn_index_attach_comm(knn_index* h, const void* uid, int n_ranks, int rank) 
   if (st != KNN_OK) return st;
   h->n_ranks = n_ranks;
   h->rank = rank;
+  return KNN_OK;
+}
+
+int knn_index_set_graphs(knn_index* h, int enabled) {
+  if (!h) return fail(KNN_EINVAL, "null index");
+  std::lock_guard<std::mutex> lock(h->mu);
+  KNN_CUDA(cudaSetDevice(h->device));
+  drop_graphs(h);
+  h->use_graphs = enabled != 0;
   return KNN_OK;
 }
 

@@ -200,6 +200,14 @@ int knn_comm_unique_id(void* out_128_bytes);
 int knn_index_attach_comm(knn_index* index, const void* unique_id_128_bytes,
                           int n_ranks, int rank);
 
+/* CUDA graphs (on by default): a search whose queries and outputs are all
+ * device memory is captured once into a CUDA graph (query conversion, scan,
+ * merge and, with a communicator, the all-gather and final merge) and
+ * replayed when later searches repeat the same buffers, sizes and stream.
+ * Rebuilding the index, changing its stream or communicator, or growing its
+ * scratch memory discards the graphs.  No counterpart in the reference. */
+int knn_index_set_graphs(knn_index* index, int enabled);
+
 /* Kernel timing: when enabled, the engine records CUDA events around its
  * fused scan kernel and its merge kernels on the stream they are launched on
  * and accumulates their durations.  No counterpart in the reference. */

@@ -172,6 +172,37 @@ def test_device_pointers_and_async(engine, oracle_mod, torch_cuda):
         assert np.array_equal(i2, i)
 
 
+def test_graph_replay_follows_buffer_contents(engine, oracle_mod, torch_cuda):
+    """Repeated device-resident searches are replayed from a CUDA graph; a
+    replay must read the current contents of the (same) query buffer and
+    match the graph-free path bit for bit."""
+    torch = torch_cuda
+    rng = np.random.Generator(np.random.PCG64(12))
+    base = rng.standard_normal((6000, 128), dtype=np.float32)
+    qa = rng.standard_normal((40, 128), dtype=np.float32)
+    qb = rng.standard_normal((40, 128), dtype=np.float32)
+    with engine.Index(0) as idx:
+        idx.build(base)
+        qd = torch.from_numpy(qa).cuda()
+        ni = torch.empty((40, 10), dtype=torch.int32, device="cuda")
+        nd = torch.empty((40, 10), dtype=torch.float32, device="cuda")
+        outs = []
+        for src in (qa, qa, qa, qb, qb, qa):
+            qd.copy_(torch.from_numpy(src))
+            idx.search_async(qd, 10, ni, nd)
+            idx.sync()
+            outs.append((ni.cpu().numpy().copy(), nd.cpu().numpy().copy()))
+        idx.set_graphs(False)
+        ref = {}
+        for name, src in (("a", qa), ("b", qb)):
+            qd.copy_(torch.from_numpy(src))
+            idx.search_async(qd, 10, ni, nd)
+            idx.sync()
+            ref[name] = (ni.cpu().numpy().copy(), nd.cpu().numpy().copy())
+    for (i, d), name in zip(outs, "aaabba"):
+        assert np.array_equal(i, ref[name][0]) and np.array_equal(d, ref[name][1])
+
+
 def test_repeat_is_bit_identical(engine, oracle_mod, torch_cuda):
     """Deterministic: two searches give the same bytes (run-twice check)."""
     rng = np.random.Generator(np.random.PCG64(9))
