@@ -35,6 +35,8 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(ROOT, "cuvs-silicon_b200")
 
+
+
 METRIC = "QPS at N=1M D=1024 K=10 Q=100 (1/2/4/8 B200) and % of HBM/tensor roofline"
 UNIT = "queries/s"
 PUBLISHED_QPS = 1012.0  # reference README.md:23-27, Apple M3 Max
@@ -53,6 +55,8 @@ def parse():
     ap.add_argument("--k", type=int, default=10)
     ap.add_argument("--centres", type=int, default=10_000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graphs", action="store_true",
+                    help="launch every search directly instead of replaying CUDA graphs")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     return a
@@ -242,7 +246,7 @@ def run_reference(a):
                          "sample": f"{sample} of {a.q} queries per step against all rows"},
         "e2e": {"value": qps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -281,6 +285,8 @@ def run_engine(a):
     torch.cuda.set_stream(stream)
     idx = E.Index(local)
     idx.set_stream(stream.cuda_stream)
+    if a.no_graphs:
+        idx.set_graphs(False)
     idx.build(shard, row_offset=lo, total_rows=a.n)
     torch.cuda.synchronize()
     host_base16 = None
@@ -417,7 +423,7 @@ def run_engine(a):
             "clocks": clk.summary(),
         }
         line.update(extra)
-        print(json.dumps(line), flush=True)
+        emit(line)
     idx.close()
     if world > 1:
         dist.barrier()
@@ -427,9 +433,30 @@ def run_engine(a):
 
 def main():
     a = parse()
+    # rank 0's stdout must carry exactly one JSON line: native libraries
+    # (NCCL's version banner, for one) write to file descriptor 1, so it
+    # points at stderr until the line is printed
+    sys.stdout.flush()
+    real_stdout = os.dup(1)
+    os.dup2(2, 1)
+    global _emit_fd
+    _emit_fd = real_stdout
     if a.impl == "reference":
         return run_reference(a)
     return run_engine(a)
+
+
+_emit_fd = None
+
+
+def emit(line: dict) -> None:
+    """Writes the result line to the real standard output."""
+    data = (json.dumps(line) + "\n").encode()
+    if _emit_fd is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_emit_fd, data)
 
 
 if __name__ == "__main__":

@@ -506,7 +506,10 @@ int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void*
     if ((st = next_profile_slot(h, &prof)) != KNN_OK) return st;
   }
   // Replay a graph for device-resident searches that repeat buffers + shape.
-  const bool graphable = h->use_graphs && !prof && cq == 1 && cn == 1 && cd == 1;
+  // Not with a communicator: replaying the captured all-gather measured
+  // slower than launching it directly (8 ranks on one NVSwitch node).
+  const bool graphable =
+      h->use_graphs && !prof && !h->comm && cq == 1 && cn == 1 && cd == 1;
   knn_index::GraphEntry* hit = nullptr;
   if (graphable) {
     for (auto& g : h->graphs) {

@@ -205,7 +205,9 @@ int knn_index_attach_comm(knn_index* index, const void* unique_id_128_bytes,
  * merge and, with a communicator, the all-gather and final merge) and
  * replayed when later searches repeat the same buffers, sizes and stream.
  * Rebuilding the index, changing its stream or communicator, or growing its
- * scratch memory discards the graphs.  No counterpart in the reference. */
+ * scratch memory discards the graphs.  Searches on an index with a
+ * communicator attached are always launched directly.  No counterpart in
+ * the reference. */
 int knn_index_set_graphs(knn_index* index, int enabled);
 
 /* Kernel timing: when enabled, the engine records CUDA events around its
