@@ -221,6 +221,13 @@ struct knn_index {
   // multi-GPU
   ncclComm_t comm = nullptr;
   int n_ranks = 1, rank = 0;
+  // peer exchange over NVLink (see knn::Exchange): own buffer, every rank's
+  // buffer as this GPU addresses it, capacity in (query, rank) list entries
+  bool peer_enabled = true;
+  float* xbuf = nullptr;
+  float* xpeer[knn::kMaxRanks] = {};
+  int64_t xcap = 0;
+  uint32_t epoch = 0;
 
   // CUDA graphs of the device-side search pipeline, replayed when a search
   // repeats the buffers and shape of a captured one.  `generation` changes
@@ -282,6 +289,104 @@ int poll_nccl(knn_index* h, double seconds) {
   }
 }
 
+int sync_stream(knn_index* h);
+void drop_exchange(knn_index* h);
+
+// Exchange buffer capacity: (query, rank) list entries; searches with more
+// queries x k use the NCCL all-gather instead.
+constexpr int64_t kExchangeCapQK = 65536;
+
+// Allocates this rank's exchange buffer, all-gathers the CUDA IPC handles
+// with NCCL and maps every peer's buffer.  On any failure the peer exchange
+// stays off (searches use the NCCL all-gather); the return value only
+// reports NCCL failures, which also break the fallback.
+int setup_exchange(knn_index* h) {
+  drop_exchange(h);
+  if (h->n_ranks > knn::kMaxRanks) return KNN_OK;
+  const int64_t words = knn::exchange_words(h->n_ranks, kExchangeCapQK);
+  cudaIpcMemHandle_t mine;
+  std::memset(&mine, 0, sizeof(mine));
+  bool ok = cudaMalloc(&h->xbuf, static_cast<size_t>(words) * 4) == cudaSuccess;
+  if (ok) ok = cudaMemset(h->xbuf, 0, static_cast<size_t>(words) * 4) == cudaSuccess;
+  if (ok) ok = cudaIpcGetMemHandle(&mine, h->xbuf) == cudaSuccess;
+  cudaGetLastError();
+  // every rank takes part in the all-gather, even with a failed allocation
+  // (a zero handle marks it), so no rank is left waiting
+  const size_t hb = sizeof(cudaIpcMemHandle_t);
+  void* dev = nullptr;
+  if (cudaMalloc(&dev, hb * (h->n_ranks + 1)) != cudaSuccess) {
+    cudaGetLastError();
+    drop_exchange(h);
+    return fail(KNN_ENOMEM, "exchange handle buffer allocation failed");
+  }
+  std::vector<cudaIpcMemHandle_t> all(h->n_ranks);
+  cudaMemcpy(static_cast<char*>(dev) + hb * h->n_ranks, &mine, hb, cudaMemcpyHostToDevice);
+  ncclResult_t r = nccl().AllGather(static_cast<char*>(dev) + hb * h->n_ranks, dev, hb,
+                                    ncclUint8, h->comm, h->stream);
+  int st = KNN_OK;
+  if (r == ncclInProgress) st = poll_nccl(h, 60.0);
+  else if (r != ncclSuccess) st = fail(KNN_ENCCL, "ncclAllGather(handles): %s", nccl_str(r));
+  if (st == KNN_OK) st = sync_stream(h);
+  if (st == KNN_OK &&
+      cudaMemcpy(all.data(), dev, hb * h->n_ranks, cudaMemcpyDeviceToHost) != cudaSuccess)
+    st = fail(KNN_ECUDA, "exchange handle copy failed");
+  cudaFree(dev);
+  if (st != KNN_OK) {
+    drop_exchange(h);
+    return st;
+  }
+  cudaIpcMemHandle_t zero;
+  std::memset(&zero, 0, sizeof(zero));
+  for (int p = 0; p < h->n_ranks && ok; ++p) {
+    if (std::memcmp(&all[p], &zero, hb) == 0) ok = false;  // that rank has no buffer
+  }
+  for (int p = 0; p < h->n_ranks && ok; ++p) {
+    if (p == h->rank) {
+      h->xpeer[p] = h->xbuf;
+      continue;
+    }
+    void* ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, all[p], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      ok = false;
+      break;
+    }
+    h->xpeer[p] = static_cast<float*>(ptr);
+  }
+  // Every rank must agree on using the exchange (a peer that could not map
+  // would otherwise never receive lists): agree through one more all-gather
+  // of the local verdict.
+  int32_t verdict = ok ? 1 : 0;
+  int32_t* vdev = nullptr;
+  if (cudaMalloc(&vdev, sizeof(int32_t) * (h->n_ranks + 1)) == cudaSuccess) {
+    cudaMemcpy(vdev + h->n_ranks, &verdict, sizeof(int32_t), cudaMemcpyHostToDevice);
+    r = nccl().AllGather(vdev + h->n_ranks, vdev, 1, ncclInt32, h->comm, h->stream);
+    st = KNN_OK;
+    if (r == ncclInProgress) st = poll_nccl(h, 60.0);
+    else if (r != ncclSuccess) st = fail(KNN_ENCCL, "ncclAllGather(verdict): %s", nccl_str(r));
+    if (st == KNN_OK) st = sync_stream(h);
+    std::vector<int32_t> v(h->n_ranks, 0);
+    if (st == KNN_OK)
+      cudaMemcpy(v.data(), vdev, sizeof(int32_t) * h->n_ranks, cudaMemcpyDeviceToHost);
+    cudaFree(vdev);
+    if (st != KNN_OK) {
+      drop_exchange(h);
+      return st;
+    }
+    for (int32_t x : v) ok = ok && x == 1;
+  } else {
+    cudaGetLastError();
+    ok = false;  // (peers then time out of nothing: they use NCCL only if all agree)
+  }
+  if (!ok) {
+    drop_exchange(h);
+    return KNN_OK;
+  }
+  h->xcap = kExchangeCapQK;
+  h->epoch = 0;
+  return KNN_OK;
+}
+
 // Waits for the index stream; with a communicator attached the wait is a
 // poll bounded by a deadline so a lost peer cannot hang the caller.
 int sync_stream(knn_index* h) {
@@ -308,6 +413,17 @@ int sync_stream(knn_index* h) {
     }
     std::this_thread::yield();
   }
+}
+
+// Closes the peer mappings and frees this rank's exchange buffer.
+void drop_exchange(knn_index* h) {
+  for (int r = 0; r < knn::kMaxRanks; ++r) {
+    if (h->xpeer[r] && h->xpeer[r] != h->xbuf) cudaIpcCloseMemHandle(h->xpeer[r]);
+    h->xpeer[r] = nullptr;
+  }
+  if (h->xbuf) cudaFree(h->xbuf);
+  h->xbuf = nullptr;
+  h->xcap = 0;
 }
 
 void drop_graphs(knn_index* h) {
@@ -417,6 +533,28 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, con
                                static_cast<int>(plan.splits), static_cast<int>(k), nq,
                                h->row_offset, dst_d, dst_i, out_i64, h->stream, overlap));
     launches += 1;
+  } else if (h->peer_enabled && h->xcap > 0 && static_cast<int64_t>(qk) <= h->xcap) {
+    // peer exchange: the local merge writes every query's list into every
+    // rank's exchange buffer over NVLink; the final merge waits for all of
+    // them (bounded) and merges from its own buffer
+    knn::Exchange ex = {};
+    for (int r = 0; r < h->n_ranks; ++r) ex.base[r] = h->xpeer[r];
+    ex.cap_qk = h->xcap;
+    ex.n_ranks = h->n_ranks;
+    ex.rank = h->rank;
+    ex.epoch = ++h->epoch;
+    ex.parity = static_cast<int>(ex.epoch & 1u);
+    ex.err = h->err_dev;
+    ex.mode = 1;
+    KNN_CUDA(knn::launch_merge(p.part_d, p.part_i, k, plan.splits * k,
+                               static_cast<int>(plan.splits), static_cast<int>(k), nq,
+                               h->row_offset, nullptr, nullptr, false, h->stream, overlap, &ex));
+    ex.mode = 2;
+    const float* rd = h->xbuf + static_cast<int64_t>(ex.parity) * h->n_ranks * 2 * h->xcap;
+    const uint32_t* ri = reinterpret_cast<const uint32_t*>(rd + h->xcap);
+    KNN_CUDA(knn::launch_merge(rd, ri, 2 * h->xcap, k, h->n_ranks, static_cast<int>(k), nq, 0,
+                               dst_d, dst_i, out_i64, h->stream, overlap, &ex));
+    launches += 2;
   } else {
     // local merge into the send buffer: [dist k floats | idx k uint32] per query
     const size_t list_bytes = qk * 8;
@@ -724,6 +862,7 @@ int knn_index_destroy(knn_index* h) {
   cudaSetDevice(h->device);
   if (h->stream) cudaStreamSynchronize(h->stream);
   drop_graphs(h);
+  drop_exchange(h);
   if (h->comm) nccl().CommDestroy(h->comm);
   for (DevBuf* b : {&h->q32, &h->q16, &h->qnorm, &h->part_d, &h->part_i, &h->out_d, &h->out_i,
                     &h->gather_send, &h->gather_recv})
@@ -873,6 +1012,7 @@ int knn_index_attach_comm(knn_index* h, const void* uid, int n_ranks, int rank) 
     nccl().CommDestroy(h->comm);
     h->comm = nullptr;
   }
+  drop_exchange(h);
   ++h->generation;
   drop_graphs(h);
   if (n_ranks == 1) {
@@ -894,6 +1034,13 @@ int knn_index_attach_comm(knn_index* h, const void* uid, int n_ranks, int rank) 
   if (st != KNN_OK) return st;
   h->n_ranks = n_ranks;
   h->rank = rank;
+  return setup_exchange(h);
+}
+
+int knn_index_set_peer_exchange(knn_index* h, int enabled) {
+  if (!h) return fail(KNN_EINVAL, "null index");
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->peer_enabled = enabled != 0;
   return KNN_OK;
 }
 

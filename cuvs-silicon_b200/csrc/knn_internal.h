@@ -78,13 +78,43 @@ inline int64_t padded_query_rows(const Plan& plan) {
 // Launches the bounded-wait self-test kernel (see knn_scan.cu).
 cudaError_t launch_bounded_wait_selftest(int* err, uint64_t limit_ns, cudaStream_t stream);
 
+// Peer exchange of per-rank top-k lists over NVLink (replaces the NCCL
+// all-gather for searches that fit).  Every rank owns one exchange buffer:
+//   data  [2 parities][n_ranks][2 * cap_qk words]: distances then indices of
+//         one rank's Q x k list (words of 4 bytes);
+//   flags [n_ranks][cap_qk] uint32: the search epoch whose list for query q
+//         from rank r has fully arrived.
+// `base[r]` is rank r's buffer as this GPU addresses it (its own allocation
+// or a CUDA IPC mapping).
+constexpr int kMaxRanks = 8;
+struct Exchange {
+  float* base[kMaxRanks];
+  int64_t cap_qk;
+  int n_ranks;
+  int rank;
+  int mode;        // 0 none; 1 push this rank's lists to every rank; 2 wait for all ranks
+  uint32_t epoch;  // increases by one per search
+  int parity;      // epoch & 1: which data half this search uses
+  int* err;        // device error word (wait timeouts)
+};
+constexpr int kErrTimeoutPeer = 7;  // a peer's list never arrived
+
+inline int64_t exchange_words(int n_ranks, int64_t cap_qk) {
+  return static_cast<int64_t>(n_ranks) * cap_qk * 5;  // 4 data words + 1 flag word
+}
+
 // Merges n_lists sorted top-k lists per query into the final top-k.
 // List l of query q starts at in_{d,i}[q * stride_query + l * stride_list].
 // Valid indices get index_offset added.  out_i is uint32 (no-neighbour =
 // UINT32_MAX) or int64 (no-neighbour = -1) per out_i64.
+// `ex` (optional) selects the peer exchange: mode 1 writes each query's
+// result into every rank's exchange buffer instead of out_d/out_i and raises
+// the query's flag there; mode 2 first waits (bounded) until every rank's
+// flag for the query has reached the epoch.
 cudaError_t launch_merge(const float* in_d, const uint32_t* in_i, int64_t stride_list,
                          int64_t stride_query, int n_lists, int k, int64_t n_queries,
                          int64_t index_offset, float* out_d, void* out_i, bool out_i64,
-                         cudaStream_t stream, bool overlap = true);
+                         cudaStream_t stream, bool overlap = true,
+                         const Exchange* ex = nullptr);
 
 }  // namespace knn

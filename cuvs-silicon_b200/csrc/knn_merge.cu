@@ -175,11 +175,12 @@ __device__ __forceinline__ void block_sort(float* d, uint32_t* i, int p2) {
   }
 }
 
-// Fold path: folds every list of query q; writes the first k entries.
-template <int E, typename OutIdx>
+// Fold path: folds every list of the query; leaves the first k entries of
+// the result in res_d / res_i (shared memory, read after a block barrier).
+template <int E>
 __device__ void fold_merge(float* sd, uint32_t* si, const float* qd, const uint32_t* qi,
-                           int64_t stride_list, int n_lists, int k, int64_t q,
-                           int64_t index_offset, float* out_d, OutIdx* out_i) {
+                           int64_t stride_list, int n_lists, int k, float* res_d,
+                           uint32_t* res_i) {
   constexpr int K2 = 32 * E;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -215,7 +216,7 @@ __device__ void fold_merge(float* sd, uint32_t* si, const float* qd, const uint3
     }
   }
   __syncthreads();
-  if (warp != 0) return;
+  if (warp == 0) {
   for (int w = 1; w < kMergeWarps && w < n_lists; ++w) {
     List<E> b;
 #pragma unroll
@@ -225,10 +226,92 @@ __device__ void fold_merge(float* sd, uint32_t* si, const float* qd, const uint3
     }
     merge_into(acc, b, lane);
   }
+  }
+  __syncthreads();  // every warp is done reading the staged lists
+  if (warp == 0) {
 #pragma unroll
-  for (int r = 0; r < E; ++r) {
-    const int e = r * 32 + lane;
-    if (e < k) store_out(out_d, out_i, q * k + e, acc.d[r], acc.i[r], index_offset);
+    for (int r = 0; r < E; ++r) {
+      const int e = r * 32 + lane;
+      if (e < k) {
+        res_d[e] = acc.d[r];
+        res_i[e] = acc.i[r];
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Mode 2: thread 0 waits (bounded, 1 s) until every rank's list for query q
+// carries this search's epoch.  Returns false (for the whole block) after
+// recording kErrTimeoutPeer when a list never arrives.
+__device__ bool wait_for_peers(const Exchange& ex, int64_t q, int* s_abort) {
+  if (threadIdx.x == 0) {
+    const uint32_t* flags = reinterpret_cast<const uint32_t*>(ex.base[ex.rank]) +
+                            static_cast<int64_t>(ex.n_ranks) * ex.cap_qk * 4;
+    int ok = 1;
+    uint64_t t0 = 0;
+    for (int r = 0; r < ex.n_ranks && ok; ++r) {
+      const uint32_t* f = flags + static_cast<int64_t>(r) * ex.cap_qk + q;
+      while (static_cast<int32_t>(ld_acquire_sys(f) - ex.epoch) < 0) {
+        uint64_t now;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+        if (t0 == 0) t0 = now;
+        if (now - t0 > 1000000000ull) {
+          atomicCAS(ex.err, 0, kErrTimeoutPeer);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    *s_abort = ok ? 0 : 1;
+  }
+  __syncthreads();
+  return *s_abort == 0;
+}
+
+// Writes the query's first k result entries (the first `count` valid, the
+// rest padding) to the output, or in mode 1 to every rank's exchange buffer
+// followed by the query's flag there.  Called by every thread of the block.
+template <typename OutIdx>
+__device__ void emit_result(const Exchange& ex, int64_t q, int k, const float* rd,
+                            const uint32_t* ri, int count, int64_t index_offset, float* out_d,
+                            OutIdx* out_i) {
+  const float kInf = __int_as_float(0x7f800000);
+  if (ex.mode != 1) {
+    for (int e = threadIdx.x; e < k; e += blockDim.x) {
+      const bool have = e < count;
+      store_out(out_d, out_i, q * k + e, have ? rd[e] : kInf, have ? ri[e] : kNoIndex,
+                index_offset);
+    }
+    return;
+  }
+  const int64_t slot = 2 * ex.cap_qk;
+  for (int r = 0; r < ex.n_ranks; ++r) {
+    float* dst = ex.base[r] + (static_cast<int64_t>(ex.parity) * ex.n_ranks + ex.rank) * slot;
+    uint32_t* dsti = reinterpret_cast<uint32_t*>(dst + ex.cap_qk);
+    for (int e = threadIdx.x; e < k; e += blockDim.x) {
+      const bool have = e < count;
+      const uint32_t idx = have ? ri[e] : kNoIndex;
+      dst[q * k + e] = have ? rd[e] : kInf;
+      dsti[q * k + e] = idx == kNoIndex ? kNoIndex : static_cast<uint32_t>(idx + index_offset);
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int r = 0; r < ex.n_ranks; ++r) {
+      uint32_t* flags = reinterpret_cast<uint32_t*>(ex.base[r]) +
+                        static_cast<int64_t>(ex.n_ranks) * ex.cap_qk * 4;
+      st_release_sys(flags + static_cast<int64_t>(ex.rank) * ex.cap_qk + q, ex.epoch);
+    }
   }
 }
 
@@ -236,14 +319,17 @@ template <int E, typename OutIdx>
 __global__ void __launch_bounds__(kMergeWarps * 32)
     merge_kernel(const float* __restrict__ in_d, const uint32_t* __restrict__ in_i,
                  int64_t stride_list, int64_t stride_query, int n_lists, int k,
-                 int64_t index_offset, float* __restrict__ out_d, OutIdx* __restrict__ out_i) {
+                 int64_t index_offset, float* __restrict__ out_d, OutIdx* __restrict__ out_i,
+                 const Exchange ex) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ uint8_t smem_raw[];
   float* sd = reinterpret_cast<float*>(smem_raw);
   uint32_t* si = reinterpret_cast<uint32_t*>(sd + kStageEntries);
   __shared__ int s_count;
+  __shared__ int s_abort;
 
   const int64_t q = blockIdx.x;
+  if (ex.mode == 2 && !wait_for_peers(ex, q, &s_abort)) return;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const float* qd = in_d + q * stride_query;
@@ -258,8 +344,9 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
   float* cd = sd + kSelCap;
   uint32_t* ci = si + kSelCap;
   if (n_lists > kSelCap) {
-    fold_merge<E, OutIdx>(sd, si, qd, qi, stride_list, n_lists, k, q, index_offset, out_d,
-                          out_i);
+    fold_merge<E>(sd, si, qd, qi, stride_list, n_lists, k, sd + kSelCap, si + kSelCap);
+    __syncthreads();
+    emit_result(ex, q, k, sd + kSelCap, si + kSelCap, k, index_offset, out_d, out_i);
     return;
   }
   int p2 = 1;
@@ -323,8 +410,9 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
   const int count = s_count;
   if (count > kCandCap) {  // block-uniform
     __syncthreads();
-    fold_merge<E, OutIdx>(sd, si, qd, qi, stride_list, n_lists, k, q, index_offset, out_d,
-                          out_i);
+    fold_merge<E>(sd, si, qd, qi, stride_list, n_lists, k, cd, ci);
+    __syncthreads();
+    emit_result(ex, q, k, cd, ci, k, index_offset, out_d, out_i);
     return;
   }
   int c2 = 1;
@@ -335,18 +423,14 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
   }
   __syncthreads();
   block_sort(cd, ci, c2);
-  for (int e = tid; e < k; e += blockDim.x) {
-    const bool have = e < count;
-    store_out(out_d, out_i, q * k + e, have ? cd[e] : kInf, have ? ci[e] : kNoIndex,
-              index_offset);
-  }
+  emit_result(ex, q, k, cd, ci, count, index_offset, out_d, out_i);
 }
 
 template <int E>
 cudaError_t launch_e(const float* in_d, const uint32_t* in_i, int64_t stride_list,
                      int64_t stride_query, int n_lists, int k, int64_t n_queries,
                      int64_t index_offset, float* out_d, void* out_i, bool out_i64,
-                     cudaStream_t stream, bool overlap) {
+                     cudaStream_t stream, bool overlap, const Exchange& ex) {
   static_assert(kMergeWarps * 32 * E <= kStageEntries, "warp lists fit the staging area");
   static_assert(kCandCap <= kStageEntries, "candidates fit the staging area");
   constexpr size_t smem = static_cast<size_t>(kStageEntries) * 8;
@@ -379,11 +463,11 @@ cudaError_t launch_e(const float* in_d, const uint32_t* in_i, int64_t stride_lis
   if (out_i64) {
     return cudaLaunchKernelEx(&cfg, merge_kernel<E, int64_t>, in_d, in_i, stride_list,
                               stride_query, n_lists, k, index_offset, out_d,
-                              static_cast<int64_t*>(out_i));
+                              static_cast<int64_t*>(out_i), ex);
   }
   return cudaLaunchKernelEx(&cfg, merge_kernel<E, uint32_t>, in_d, in_i, stride_list,
                             stride_query, n_lists, k, index_offset, out_d,
-                            static_cast<uint32_t*>(out_i));
+                            static_cast<uint32_t*>(out_i), ex);
 }
 
 }  // namespace
@@ -391,21 +475,23 @@ cudaError_t launch_e(const float* in_d, const uint32_t* in_i, int64_t stride_lis
 cudaError_t launch_merge(const float* in_d, const uint32_t* in_i, int64_t stride_list,
                          int64_t stride_query, int n_lists, int k, int64_t n_queries,
                          int64_t index_offset, float* out_d, void* out_i, bool out_i64,
-                         cudaStream_t stream, bool overlap) {
+                         cudaStream_t stream, bool overlap, const Exchange* ex_opt) {
   if (n_queries <= 0 || k <= 0) return cudaSuccess;
+  Exchange none = {};
+  const Exchange& ex = ex_opt ? *ex_opt : none;
   if (n_queries > 0x7fffffff) return cudaErrorInvalidValue;
   if (k <= 32)
     return launch_e<1>(in_d, in_i, stride_list, stride_query, n_lists, k, n_queries,
-                       index_offset, out_d, out_i, out_i64, stream, overlap);
+                       index_offset, out_d, out_i, out_i64, stream, overlap, ex);
   if (k <= 64)
     return launch_e<2>(in_d, in_i, stride_list, stride_query, n_lists, k, n_queries,
-                       index_offset, out_d, out_i, out_i64, stream, overlap);
+                       index_offset, out_d, out_i, out_i64, stream, overlap, ex);
   if (k <= 128)
     return launch_e<4>(in_d, in_i, stride_list, stride_query, n_lists, k, n_queries,
-                       index_offset, out_d, out_i, out_i64, stream, overlap);
+                       index_offset, out_d, out_i, out_i64, stream, overlap, ex);
   if (k <= 256)
     return launch_e<8>(in_d, in_i, stride_list, stride_query, n_lists, k, n_queries,
-                       index_offset, out_d, out_i, out_i64, stream, overlap);
+                       index_offset, out_d, out_i, out_i64, stream, overlap, ex);
   return cudaErrorInvalidValue;
 }
 

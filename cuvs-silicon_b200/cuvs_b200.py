@@ -83,6 +83,7 @@ def lib() -> ctypes.CDLL:
         "knn_index_attach_comm": (I, [P, P, I, I]),
         "knn_index_set_profiling": (I, [P, I]),
         "knn_index_set_graphs": (I, [P, I]),
+        "knn_index_set_peer_exchange": (I, [P, I]),
         "knn_index_kernel_stats": (I, [P, ctypes.POINTER(ctypes.c_double),
                                        ctypes.POINTER(ctypes.c_double),
                                        ctypes.POINTER(I64), ctypes.POINTER(I64)]),
@@ -266,6 +267,9 @@ class Index:
 
     def sync(self) -> None:
         _check(lib().knn_index_sync(self._h))
+
+    def set_peer_exchange(self, on: bool) -> None:
+        _check(lib().knn_index_set_peer_exchange(self._h, 1 if on else 0))
 
     def set_graphs(self, on: bool) -> None:
         _check(lib().knn_index_set_graphs(self._h, 1 if on else 0))

@@ -210,6 +210,16 @@ int knn_index_attach_comm(knn_index* index, const void* unique_id_128_bytes,
  * the reference. */
 int knn_index_set_graphs(knn_index* index, int enabled);
 
+/* Peer exchange (on by default when every rank could map every other
+ * rank's exchange buffer at knn_index_attach_comm): the per-rank top-k
+ * lists of a search travel as direct NVLink stores into every rank's
+ * buffer, each query's list followed by an epoch flag, and the final merge
+ * waits (bounded, 1 s) for the flags.  Searches with more than 65,536
+ * query x k entries, and indexes with the exchange off, use the NCCL
+ * all-gather.  Every rank must make the same choice.  No counterpart in the
+ * reference. */
+int knn_index_set_peer_exchange(knn_index* index, int enabled);
+
 /* Kernel timing: when enabled, the engine records CUDA events around its
  * fused scan kernel and its merge kernels on the stream they are launched on
  * and accumulates their durations.  No counterpart in the reference. */

@@ -87,11 +87,32 @@ def main():
             qd = torch.from_numpy(queries).cuda()
             ni = torch.empty((nq, 10), dtype=torch.int32, device="cuda")
             nd = torch.empty((nq, 10), dtype=torch.float32, device="cuda")
-            ref_i, _ = idx.search(queries, 10)
+            ref_i, ref_d = idx.search(queries, 10)
             for _ in range(2):
                 idx.search_async(qd, 10, ni, nd)
                 idx.sync()
                 assert np.array_equal(ni.cpu().numpy().view(np.uint32), ref_i)
+            # the NCCL all-gather fallback gives the same bytes
+            idx.set_peer_exchange(False)
+            gi, gd = idx.search(queries, 10)
+            assert np.array_equal(gi, ref_i) and np.array_equal(gd, ref_d)
+            idx.set_peer_exchange(True)
+            gi, gd = idx.search(queries, 10)
+            assert np.array_equal(gi, ref_i) and np.array_equal(gd, ref_d)
+            dist.barrier()
+            # failure detection: rank 1 skips this search, so rank 0's final
+            # merge waits for lists that never come; its bounded wait must
+            # give up and report KNN_ETIMEOUT (the GPU stays usable)
+            if rank == 0:
+                try:
+                    idx.search(queries, 10)
+                    print("rank 0: search without its peer did not time out", flush=True)
+                    return 1
+                except RuntimeError as e:
+                    assert "ETIMEOUT" in str(e), str(e)
+                    print("rank 0 detected the missing peer list", flush=True)
+                torch.cuda.synchronize()
+            dist.barrier()
         dist.barrier()
         dist.destroy_process_group()
         return 0

@@ -59,3 +59,4 @@ def test_gpu_two_ranks_nccl(engine):
         pytest.skip("needs 2 GPUs")
     rc, out = _launch("gpu", 2, 600)
     assert rc == 0, out[-4000:]
+    assert "detected the missing peer list" in out, out[-4000:]
