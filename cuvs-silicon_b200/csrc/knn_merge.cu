@@ -175,6 +175,29 @@ __device__ __forceinline__ void block_sort(float* d, uint32_t* i, int p2) {
   }
 }
 
+// Sorts n <= blockDim.x entries by rank counting: thread t takes entry t,
+// counts the entries ordered before it (one broadcast shared-memory read per
+// entry, no barrier in between) and stores it at that rank in out_d/out_i,
+// which must not alias in_d/in_i.  Keys are distinct except for padding
+// entries, which land on the positions their rank gives (all padding values
+// are equal, so any of them may fill those slots); only ranks < limit are
+// stored.  Called by every thread; ends with a block barrier.
+__device__ __forceinline__ void rank_place(const float* in_d, const uint32_t* in_i, int n,
+                                           float* out_d, uint32_t* out_i, int limit) {
+  const int t = threadIdx.x;
+  if (t < n) {
+    const float d = in_d[t];
+    const uint32_t i = in_i[t];
+    int rank = 0;
+    for (int u = 0; u < n; ++u) rank += less_pair(in_d[u], in_i[u], d, i) ? 1 : 0;
+    if (rank < limit) {
+      out_d[rank] = d;
+      out_i[rank] = i;
+    }
+  }
+  __syncthreads();
+}
+
 // Fold path: folds every list of the query; leaves the first k entries of
 // the result in res_d / res_i (shared memory, read after a block barrier).
 template <int E>
@@ -363,9 +386,34 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
   }
   if (tid == 0) s_count = 0;
   __syncthreads();
-  block_sort(seld, seli, p2);
-  const float td = seld[r - 1];
-  const uint32_t ti = seli[r - 1];
+  float td;
+  uint32_t ti;
+  if (n_lists <= static_cast<int>(blockDim.x)) {
+    // rank counting: the entry of rank r - 1 is tau (cd/ci are free here)
+    if (tid == 0) {
+      cd[0] = kInf;
+      ci[0] = kNoIndex;
+    }
+    __syncthreads();
+    if (tid < n_lists) {
+      const float d = seld[tid];
+      const uint32_t i = seli[tid];
+      int rank = 0;
+      for (int u = 0; u < n_lists; ++u) rank += less_pair(seld[u], seli[u], d, i) ? 1 : 0;
+      if (rank == r - 1) {
+        cd[0] = d;
+        ci[0] = i;
+      }
+    }
+    __syncthreads();
+    td = cd[0];
+    ti = ci[0];
+    __syncthreads();
+  } else {
+    block_sort(seld, seli, p2);
+    td = seld[r - 1];
+    ti = seli[r - 1];
+  }
 
   // candidates: every valid entry (d, i) <= tau (every valid entry when
   // tau is the padding, i.e. when fewer than r lists have j entries)
@@ -415,6 +463,13 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
     emit_result(ex, q, k, cd, ci, k, index_offset, out_d, out_i);
     return;
   }
+  if (count <= static_cast<int>(blockDim.x)) {
+    // candidates are distinct (distinct row indices): rank counting places
+    // the first k of them, sorted, in front of the selection array
+    rank_place(cd, ci, count, seld, seli, k);
+    emit_result(ex, q, k, seld, seli, count, index_offset, out_d, out_i);
+    return;
+  }
   int c2 = 1;
   while (c2 < count) c2 <<= 1;
   for (int e = count + tid; e < c2; e += blockDim.x) {
@@ -447,6 +502,13 @@ cudaError_t launch_e(const float* in_d, const uint32_t* in_i, int64_t stride_lis
                 : cudaFuncSetAttribute(merge_kernel<E, uint32_t>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    // same shared-memory carve-out as the scan kernel: no SM reconfiguration
+    // between the two
+    e = out_i64 ? cudaFuncSetAttribute(merge_kernel<E, int64_t>,
+                                       cudaFuncAttributePreferredSharedMemoryCarveout, 100)
+                : cudaFuncSetAttribute(merge_kernel<E, uint32_t>,
+                                       cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev][w] = true;
   }

@@ -38,6 +38,9 @@ template <bool kHalfIn>
 __global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, int64_t rows_out,
                                     int64_t dim, __half* __restrict__ out, int64_t ld,
                                     float* __restrict__ norms, bool vec) {
+  // launched as a programmatic dependent of the previous search's kernels,
+  // which may still read `out`: wait for them before writing
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane = threadIdx.x & 31;
   const int64_t warps_per_block = blockDim.x >> 5;
   const int64_t first = static_cast<int64_t>(blockIdx.x) * warps_per_block + (threadIdx.x >> 5);
@@ -114,14 +117,20 @@ cudaError_t launch_convert_rows(const void* in, bool in_is_half, int64_t rows, i
   const int64_t warps_needed = rows_out;
   int64_t blocks = (warps_needed + (kThreads / 32) - 1) / (kThreads / 32);
   if (blocks > 148 * 16) blocks = 148 * 16;
-  if (in_is_half) {
-    convert_rows_kernel<true><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
-        in, rows, rows_out, dim, out, ld, norms, vec);
-  } else {
-    convert_rows_kernel<false><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
-        in, rows, rows_out, dim, out, ld, norms, vec);
-  }
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (in_is_half)
+    return cudaLaunchKernelEx(&cfg, convert_rows_kernel<true>, in, rows, rows_out, dim, out, ld,
+                              norms, vec);
+  return cudaLaunchKernelEx(&cfg, convert_rows_kernel<false>, in, rows, rows_out, dim, out, ld,
+                            norms, vec);
 }
 
 }  // namespace knn
