@@ -213,8 +213,18 @@ struct knn_index {
   float* norms = nullptr;
   CUtensorMap xmap;
 
+  // exact fp32 re-ranking (knn_index_set_rerank): the fp32 rows are kept
+  // by a build made while re-ranking is enabled
+  bool rerank = false;
+  float* rows32 = nullptr;     // n x dim fp32 rows
+  float* max_norm2 = nullptr;  // device scalar: largest |x16|^2
+  int* uncert_dev = nullptr;
+  int* uncert_host = nullptr;  // pinned
+  int64_t last_uncertified = 0, last_widened = 0;
+
   // per-search scratch
   DevBuf q32, q16, qnorm, part_d, part_i, out_d, out_i, gather_send, gather_recv;
+  DevBuf cand_d, cand_i, rr_d, rr_i;
   int* err_dev = nullptr;
   int* err_host = nullptr;  // pinned
 
@@ -237,7 +247,7 @@ struct knn_index {
     const void* queries;
     const void* neighbors;
     const void* distances;
-    int64_t nq, k;
+    int64_t nq, k, ks;
     bool i64;
     cudaStream_t stream;
     uint64_t generation;
@@ -491,12 +501,17 @@ int validate_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
 // Everything a search enqueues on the device between the query upload and
 // the result download: query conversion, scan, merge(s) and the all-gather.
 // Captured into a CUDA graph when the search is replayable.
-int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, const Plan& plan,
-                     float* dst_d, void* dst_i, bool out_i64,
+// With re-ranking, the scan keeps ks > k candidates per query, a merge
+// orders them, and the re-rank kernel replaces the scan's distances by the
+// exact fp32 ones; the k-lists it writes then take the place of the scan's
+// per-unit lists in the exchange between ranks.
+int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int64_t ks,
+                     bool rerank, const Plan& plan, float* dst_d, void* dst_i, bool out_i64,
                      std::array<cudaEvent_t, 3>* prof, int* launches_out) {
   int st;
   const size_t qk = static_cast<size_t>(nq) * k;
   const int64_t nq_pad = knn::padded_query_rows(plan);
+  if (rerank) KNN_CUDA(cudaMemsetAsync(h->uncert_dev, 0, sizeof(int), h->stream));
   KNN_CUDA(knn::launch_convert_rows(qsrc, false, nq, nq_pad, h->dim, h->q16.as<__half>(),
                                     h->ld, h->qnorm.as<float>(), h->stream));
   CUtensorMap qmap;
@@ -512,7 +527,7 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, con
   p.n_rows = h->n;
   p.n_queries = nq;
   p.row_tiles = plan.row_tiles;
-  p.k = static_cast<int32_t>(k);
+  p.k = static_cast<int32_t>(ks);
   p.query_block = static_cast<int32_t>(plan.query_block);
   p.query_tiles = static_cast<int32_t>(plan.query_tiles);
   p.splits = static_cast<int32_t>(plan.splits);
@@ -520,6 +535,8 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, con
   p.k_chunks = static_cast<int32_t>((h->ld + knn::kKChunk - 1) / knn::kKChunk);
   p.stages = static_cast<int32_t>(plan.stages);
   p.dataset_evict_first = plan.query_tiles == 1 ? 1 : 0;
+  p.metric = h->metric;
+  const bool neg = h->metric == KNN_METRIC_INNER_PRODUCT;
 
   if (prof) KNN_CUDA(cudaEventRecord((*prof)[0], h->stream));
   // with timing events between kernels, launch them plainly serialised
@@ -528,10 +545,44 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, con
   if (prof) KNN_CUDA(cudaEventRecord((*prof)[1], h->stream));
 
   int launches = 2;
+  // the lists the final stage merges: the scan's per-unit lists, or one
+  // re-ranked list per query
+  const float* ld = p.part_d;
+  const uint32_t* li = p.part_i;
+  int64_t l_stride = ks, q_stride = plan.splits * ks, off = h->row_offset;
+  int n_lists = static_cast<int>(plan.splits);
+  if (rerank) {
+    float* cd = h->cand_d.as<float>();
+    uint32_t* ci = h->cand_i.as<uint32_t>();
+    KNN_CUDA(knn::launch_merge(p.part_d, p.part_i, ks, plan.splits * ks,
+                               static_cast<int>(plan.splits), static_cast<int>(ks), nq, 0, cd,
+                               ci, false, h->stream, overlap));
+    if (!h->comm) {
+      KNN_CUDA(knn::launch_rerank(qsrc, h->rows32, h->dim, cd, ci, static_cast<int>(ks),
+                                  static_cast<int>(k), nq, h->metric, h->max_norm2,
+                                  h->row_offset, dst_d, dst_i, out_i64, neg, h->uncert_dev,
+                                  h->stream));
+      if (prof) KNN_CUDA(cudaEventRecord((*prof)[2], h->stream));
+      *launches_out = launches + 2;
+      return KNN_OK;
+    }
+    float* rd = h->rr_d.as<float>();
+    uint32_t* ri = h->rr_i.as<uint32_t>();
+    KNN_CUDA(knn::launch_rerank(qsrc, h->rows32, h->dim, cd, ci, static_cast<int>(ks),
+                                static_cast<int>(k), nq, h->metric, h->max_norm2,
+                                h->row_offset, rd, ri, false, false, h->uncert_dev,
+                                h->stream));
+    launches += 2;
+    ld = rd;
+    li = ri;
+    l_stride = k;
+    q_stride = k;
+    n_lists = 1;
+    off = 0;
+  }
   if (!h->comm) {
-    KNN_CUDA(knn::launch_merge(p.part_d, p.part_i, k, plan.splits * k,
-                               static_cast<int>(plan.splits), static_cast<int>(k), nq,
-                               h->row_offset, dst_d, dst_i, out_i64, h->stream, overlap));
+    KNN_CUDA(knn::launch_merge(ld, li, l_stride, q_stride, n_lists, static_cast<int>(k), nq,
+                               off, dst_d, dst_i, out_i64, h->stream, overlap, nullptr, neg));
     launches += 1;
   } else if (h->peer_enabled && h->xcap > 0 && static_cast<int64_t>(qk) <= h->xcap) {
     // peer exchange: the local merge writes every query's list into every
@@ -546,23 +597,21 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, con
     ex.parity = static_cast<int>(ex.epoch & 1u);
     ex.err = h->err_dev;
     ex.mode = 1;
-    KNN_CUDA(knn::launch_merge(p.part_d, p.part_i, k, plan.splits * k,
-                               static_cast<int>(plan.splits), static_cast<int>(k), nq,
-                               h->row_offset, nullptr, nullptr, false, h->stream, overlap, &ex));
+    KNN_CUDA(knn::launch_merge(ld, li, l_stride, q_stride, n_lists, static_cast<int>(k), nq, off,
+                               nullptr, nullptr, false, h->stream, overlap, &ex));
     ex.mode = 2;
     const float* rd = h->xbuf + static_cast<int64_t>(ex.parity) * h->n_ranks * 2 * h->xcap;
     const uint32_t* ri = reinterpret_cast<const uint32_t*>(rd + h->xcap);
     KNN_CUDA(knn::launch_merge(rd, ri, 2 * h->xcap, k, h->n_ranks, static_cast<int>(k), nq, 0,
-                               dst_d, dst_i, out_i64, h->stream, overlap, &ex));
+                               dst_d, dst_i, out_i64, h->stream, overlap, &ex, neg));
     launches += 2;
   } else {
     // local merge into the send buffer: [dist k floats | idx k uint32] per query
     const size_t list_bytes = qk * 8;
     float* send_d = h->gather_send.as<float>();
     uint32_t* send_i = reinterpret_cast<uint32_t*>(send_d + qk);
-    KNN_CUDA(knn::launch_merge(p.part_d, p.part_i, k, plan.splits * k,
-                               static_cast<int>(plan.splits), static_cast<int>(k), nq,
-                               h->row_offset, send_d, send_i, false, h->stream, overlap));
+    KNN_CUDA(knn::launch_merge(ld, li, l_stride, q_stride, n_lists, static_cast<int>(k), nq, off,
+                               send_d, send_i, false, h->stream, overlap));
     ncclResult_t r = nccl().AllGather(h->gather_send.ptr, h->gather_recv.ptr, list_bytes,
                                       ncclUint8, h->comm, h->stream);
     if (r == ncclInProgress) {
@@ -575,7 +624,7 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, con
     const uint32_t* ri = reinterpret_cast<const uint32_t*>(rd + qk);
     KNN_CUDA(knn::launch_merge(rd, ri, static_cast<int64_t>(2 * qk), k, h->n_ranks,
                                static_cast<int>(k), nq, 0, dst_d, dst_i, out_i64, h->stream,
-                               overlap));
+                               overlap, nullptr, neg));
     launches += 2;
   }
   if (prof) KNN_CUDA(cudaEventRecord((*prof)[2], h->stream));
@@ -583,32 +632,24 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, con
   return KNN_OK;
 }
 
-// Core search.  out_i64: neighbours are int64.  sync: block and check.
-int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void* neighbors,
-                float* distances, bool out_i64, bool sync, bool require_device) {
-  int st = validate_search(h, queries, nq, k, neighbors, distances);
-  if (st != KNN_OK || nq == 0 || k == 0) return st;
-  std::lock_guard<std::mutex> lock(h->mu);
-  KNN_CUDA(cudaSetDevice(h->device));
-
-  const int cq = classify(queries, h->device);
-  const int cn = classify(neighbors, h->device);
-  const int cd = classify(distances, h->device);
-  if (cq < 0 || cn < 0 || cd < 0)
-    return fail(KNN_EINVAL, "buffer lives on a different device than the index");
-  if (require_device && (cq == 0 || cn == 0 || cd == 0))
-    return fail(KNN_EINVAL, "knn_index_search_async requires device buffers");
-
+// One search pass (h->mu held, device set, buffers classified: cq/cn/cd are
+// 1 for device and 0 for host memory).  ks: candidates the scan keeps per
+// query (k, or more when re-ranking).
+int search_pass(knn_index* h, const float* queries, int64_t nq, int64_t k, int64_t ks,
+                bool rerank, void* neighbors, float* distances, bool out_i64, bool sync,
+                int cq, int cn, int cd) {
+  int st;
   Plan plan;
-  const int pst = knn::plan_search(h->n, h->dim, nq, k, h->num_sms, &plan);
-  if (pst != 0) return fail(pst, "k = %lld is outside the engine's limits", (long long)k);
+  const int pst = knn::plan_search(h->n, h->dim, nq, ks, h->num_sms, &plan);
+  if (pst != 0) return fail(pst, "k = %lld is outside the engine's limits", (long long)ks);
 
   // scratch: everything is sized before any work is enqueued or captured
   const size_t qk = static_cast<size_t>(nq) * k;
   const size_t idx_bytes = qk * (out_i64 ? 8 : 4);
   const int64_t nq_pad = knn::padded_query_rows(plan);
-  DevBuf* bufs[] = {&h->q16, &h->qnorm, &h->part_d, &h->part_i, &h->q32,
-                    &h->out_d, &h->out_i, &h->gather_send, &h->gather_recv};
+  DevBuf* bufs[] = {&h->q16,    &h->qnorm,       &h->part_d,      &h->part_i,
+                    &h->q32,    &h->out_d,       &h->out_i,       &h->gather_send,
+                    &h->gather_recv, &h->cand_d, &h->cand_i, &h->rr_d, &h->rr_i};
   for (DevBuf* b : bufs) b->grew = false;
   if ((st = h->q16.ensure(static_cast<size_t>(nq_pad) * h->ld * 2)) != KNN_OK) return st;
   if ((st = h->qnorm.ensure(static_cast<size_t>(nq) * 4)) != KNN_OK) return st;
@@ -620,6 +661,13 @@ int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void*
   if (h->comm) {
     if ((st = h->gather_send.ensure(qk * 8)) != KNN_OK) return st;
     if ((st = h->gather_recv.ensure(qk * 8 * h->n_ranks)) != KNN_OK) return st;
+  }
+  if (rerank) {
+    const size_t qks = static_cast<size_t>(nq) * ks;
+    if ((st = h->cand_d.ensure(qks * 4)) != KNN_OK) return st;
+    if ((st = h->cand_i.ensure(qks * 4)) != KNN_OK) return st;
+    if (h->comm && (st = h->rr_d.ensure(qk * 4)) != KNN_OK) return st;
+    if (h->comm && (st = h->rr_i.ensure(qk * 4)) != KNN_OK) return st;
   }
   for (DevBuf* b : bufs) {
     if (b->grew) {
@@ -652,7 +700,7 @@ int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void*
   if (graphable) {
     for (auto& g : h->graphs) {
       if (g.queries == queries && g.neighbors == neighbors && g.distances == distances &&
-          g.nq == nq && g.k == k && g.i64 == out_i64 && g.stream == h->stream &&
+          g.nq == nq && g.k == k && g.ks == ks && g.i64 == out_i64 && g.stream == h->stream &&
           g.generation == h->generation) {
         hit = &g;
         break;
@@ -668,7 +716,7 @@ int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void*
         if (h->graphs.front().exec) cudaGraphExecDestroy(h->graphs.front().exec);
         h->graphs.erase(h->graphs.begin());
       }
-      h->graphs.push_back({queries, neighbors, distances, nq, k, out_i64, h->stream,
+      h->graphs.push_back({queries, neighbors, distances, nq, k, ks, out_i64, h->stream,
                            h->generation, 0, nullptr});
       goto direct;
     }
@@ -679,7 +727,8 @@ int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void*
                 cudaSuccess;
       int cst = KNN_OK;
       if (ok) {
-        cst = enqueue_pipeline(h, qsrc, nq, k, plan, dst_d, dst_i, out_i64, nullptr, &launches);
+        cst = enqueue_pipeline(h, qsrc, nq, k, ks, rerank, plan, dst_d, dst_i, out_i64, nullptr,
+                               &launches);
         ok = cudaStreamEndCapture(h->stream, &graph) == cudaSuccess && cst == KNN_OK;
       }
       if (ok) ok = cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
@@ -690,7 +739,7 @@ int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void*
           if (h->graphs.front().exec) cudaGraphExecDestroy(h->graphs.front().exec);
           h->graphs.erase(h->graphs.begin());
         }
-        h->graphs.push_back({queries, neighbors, distances, nq, k, out_i64, h->stream,
+        h->graphs.push_back({queries, neighbors, distances, nq, k, ks, out_i64, h->stream,
                              h->generation, launches, exec});
         hit = &h->graphs.back();
       } else {
@@ -706,10 +755,13 @@ direct:
     KNN_CUDA(cudaGraphLaunch(hit->exec, h->stream));
     launches = hit->launches;
   } else {
-    if ((st = enqueue_pipeline(h, qsrc, nq, k, plan, dst_d, dst_i, out_i64, prof,
+    if ((st = enqueue_pipeline(h, qsrc, nq, k, ks, rerank, plan, dst_d, dst_i, out_i64, prof,
                                &launches)) != KNN_OK)
       return st;
   }
+  if (rerank)
+    KNN_CUDA(cudaMemcpyAsync(h->uncert_host, h->uncert_dev, sizeof(int), cudaMemcpyDeviceToHost,
+                             h->stream));
 
   if (cd == 0)
     KNN_CUDA(cudaMemcpyAsync(distances, dst_d, qk * 4, cudaMemcpyDeviceToHost, h->stream));
@@ -723,15 +775,48 @@ direct:
   KNN_CUDA(cudaMemcpyAsync(h->err_host, h->err_dev, sizeof(int), cudaMemcpyDeviceToHost,
                            h->stream));
   if ((st = sync_stream(h)) != KNN_OK) return st;
+  if (rerank) h->last_uncertified = *h->uncert_host;
   return check_device_error(h);
+}
+
+// Core search.  out_i64: neighbours are int64.  sync: block and check.
+// A blocking re-ranked search on one device whose result is not certified
+// for some query is repeated once with the largest candidate count.
+int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void* neighbors,
+                float* distances, bool out_i64, bool sync, bool require_device) {
+  int st = validate_search(h, queries, nq, k, neighbors, distances);
+  if (st != KNN_OK || nq == 0 || k == 0) return st;
+  std::lock_guard<std::mutex> lock(h->mu);
+  KNN_CUDA(cudaSetDevice(h->device));
+
+  const int cq = classify(queries, h->device);
+  const int cn = classify(neighbors, h->device);
+  const int cd = classify(distances, h->device);
+  if (cq < 0 || cn < 0 || cd < 0)
+    return fail(KNN_EINVAL, "buffer lives on a different device than the index");
+  if (require_device && (cq == 0 || cn == 0 || cd == 0))
+    return fail(KNN_EINVAL, "knn_index_search_async requires device buffers");
+
+  const bool rerank = h->rerank && h->rows32;
+  int64_t ks = rerank ? knn::rerank_candidates(k) : k;
+  h->last_widened = 0;
+  while (true) {
+    st = search_pass(h, queries, nq, k, ks, rerank, neighbors, distances, out_i64, sync, cq, cn,
+                     cd);
+    if (st != KNN_OK || !sync || !rerank || h->last_uncertified == 0 || h->comm ||
+        ks >= knn::kMaxK)
+      return st;
+    h->last_widened = h->last_uncertified;
+    ks = knn::kMaxK;
+  }
 }
 
 int build_impl(knn_index* h, const void* rows, int dtype, int64_t n, int64_t dim, int metric,
                int64_t row_offset, int64_t total_rows) {
   if (!h) return fail(KNN_EINVAL, "null index");
   // reference: src/cagra.cpp:26-28
-  if (metric != KNN_METRIC_L2_EXPANDED)
-    return fail(KNN_EINVAL, "only the L2Expanded metric is supported");
+  if (metric != KNN_METRIC_L2_EXPANDED && metric != KNN_METRIC_INNER_PRODUCT)
+    return fail(KNN_EINVAL, "metric %d is not L2Expanded (0) or InnerProduct (1)", metric);
   // reference: src/cagra.cpp:29-32
   if (!rows || n <= 0 || dim <= 0)
     return fail(KNN_EINVAL, "build requires a non-empty dataset");
@@ -751,17 +836,31 @@ int build_impl(knn_index* h, const void* rows, int dtype, int64_t n, int64_t dim
   const int where = classify(rows, h->device);
   if (where < 0) return fail(KNN_EINVAL, "dataset lives on a different device than the index");
 
+  if (h->rerank && dtype != KNN_DTYPE_F32)
+    return fail(KNN_EINVAL, "re-ranking keeps the fp32 rows: build from fp32 rows");
+
   if (h->data) cudaFree(h->data);
   if (h->norms) cudaFree(h->norms);
+  if (h->rows32) cudaFree(h->rows32);
   h->data = nullptr;
   h->norms = nullptr;
+  h->rows32 = nullptr;
   h->n = 0;
 
   const int64_t ld = row_ld(dim);
   KNN_CUDA(cudaMalloc(&h->data, static_cast<size_t>(n) * ld * 2));
   KNN_CUDA(cudaMalloc(&h->norms, static_cast<size_t>(n) * 4));
   const size_t esz = dtype == KNN_DTYPE_F16 ? 2 : 4;
-  if (where == 1) {
+  if (h->rerank) {
+    // keep the fp32 rows on the device and convert from that copy
+    KNN_CUDA(cudaMalloc(&h->rows32, static_cast<size_t>(n) * dim * 4));
+    KNN_CUDA(cudaMemcpyAsync(h->rows32, rows, static_cast<size_t>(n) * dim * 4, cudaMemcpyDefault,
+                             h->stream));
+    KNN_CUDA(knn::launch_convert_rows(h->rows32, false, n, n, dim, h->data, ld, h->norms,
+                                      h->stream));
+    KNN_CUDA(knn::launch_max_norm(h->norms, n, h->max_norm2, h->stream));
+    g_dispatch.fetch_add(2);
+  } else if (where == 1) {
     KNN_CUDA(knn::launch_convert_rows(rows, dtype == KNN_DTYPE_F16, n, n, dim, h->data, ld,
                                       h->norms, h->stream));
     g_dispatch.fetch_add(1);
@@ -846,12 +945,16 @@ int knn_index_create(int device, knn_index** out) {
   if (e == cudaSuccess) e = cudaMalloc(&h->err_dev, sizeof(int));
   if (e == cudaSuccess) e = cudaMemset(h->err_dev, 0, sizeof(int));
   if (e == cudaSuccess) e = cudaMallocHost(&h->err_host, sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&h->uncert_dev, sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&h->max_norm2, sizeof(float));
+  if (e == cudaSuccess) e = cudaMallocHost(&h->uncert_host, sizeof(int));
   for (int i = 0; i < 4 && e == cudaSuccess; ++i) e = cudaEventCreate(&h->ev[i]);
   if (e != cudaSuccess) {
     knn_index_destroy(h);
     return fail(KNN_ECUDA, "index setup: %s", cudaGetErrorString(e));
   }
   *h->err_host = 0;
+  *h->uncert_host = 0;
   h->stream = h->own_stream;
   *out = h;
   return KNN_OK;
@@ -865,10 +968,15 @@ int knn_index_destroy(knn_index* h) {
   drop_exchange(h);
   if (h->comm) nccl().CommDestroy(h->comm);
   for (DevBuf* b : {&h->q32, &h->q16, &h->qnorm, &h->part_d, &h->part_i, &h->out_d, &h->out_i,
-                    &h->gather_send, &h->gather_recv})
+                    &h->gather_send, &h->gather_recv, &h->cand_d, &h->cand_i, &h->rr_d,
+                    &h->rr_i})
     b->release();
   if (h->data) cudaFree(h->data);
   if (h->norms) cudaFree(h->norms);
+  if (h->rows32) cudaFree(h->rows32);
+  if (h->max_norm2) cudaFree(h->max_norm2);
+  if (h->uncert_dev) cudaFree(h->uncert_dev);
+  if (h->uncert_host) cudaFreeHost(h->uncert_host);
   if (h->err_dev) cudaFree(h->err_dev);
   if (h->err_host) cudaFreeHost(h->err_host);
   for (auto& ev : h->ev)
@@ -909,6 +1017,13 @@ int knn_index_copy_rows(knn_index* h, void* out, int dtype) {
     KNN_CUDA(cudaMemcpy2DAsync(out, static_cast<size_t>(h->dim) * 2, h->data,
                                static_cast<size_t>(h->ld) * 2, static_cast<size_t>(h->dim) * 2,
                                static_cast<size_t>(h->n), cudaMemcpyDefault, h->stream));
+    KNN_CUDA(cudaStreamSynchronize(h->stream));
+    return KNN_OK;
+  }
+  if (h->rows32) {
+    // the fp32 rows as given to the build
+    KNN_CUDA(cudaMemcpyAsync(out, h->rows32, static_cast<size_t>(h->n) * h->dim * 4,
+                             cudaMemcpyDefault, h->stream));
     KNN_CUDA(cudaStreamSynchronize(h->stream));
     return KNN_OK;
   }
@@ -956,7 +1071,36 @@ int knn_index_sync(knn_index* h) {
                            h->stream));
   int st = sync_stream(h);
   if (st != KNN_OK) return st;
+  if (h->rerank && h->rows32) h->last_uncertified = *h->uncert_host;
   return check_device_error(h);
+}
+
+int knn_index_set_rerank(knn_index* h, int enabled) {
+  if (!h) return fail(KNN_EINVAL, "null index");
+  std::lock_guard<std::mutex> lock(h->mu);
+  KNN_CUDA(cudaSetDevice(h->device));
+  h->rerank = enabled != 0;
+  if (!h->rerank && h->rows32) {
+    KNN_CUDA(cudaStreamSynchronize(h->stream));
+    cudaFree(h->rows32);
+    h->rows32 = nullptr;
+  }
+  h->last_uncertified = 0;
+  h->last_widened = 0;
+  ++h->generation;
+  drop_graphs(h);
+  if (h->rerank && h->data && !h->rows32)
+    return fail(KNN_EINVAL,
+                "the index was built without its fp32 rows: build it again to re-rank");
+  return KNN_OK;
+}
+
+int knn_index_rerank_stats(knn_index* h, int64_t* uncertified, int64_t* widened) {
+  if (!h) return fail(KNN_EINVAL, "null index");
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (uncertified) *uncertified = h->last_uncertified;
+  if (widened) *widened = h->last_widened;
+  return KNN_OK;
 }
 
 int knn_plan_search(int64_t n_rows, int64_t dim, int64_t nq, int64_t k, int num_sms,
@@ -1149,6 +1293,7 @@ int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
   int st = validate_search(h, queries, nq, k, neighbors, distances);
   if (st != KNN_OK || nq == 0 || k == 0) return st;
   if (h->comm) return fail(KNN_EUNSUPPORTED, "the no-allocation search does not run on a communicator");
+  if (h->rerank) return fail(KNN_EUNSUPPORTED, "the no-allocation search does not re-rank");
   if (h->device < 0 || h->device >= kNoAllocMaxDevices)
     return fail(KNN_EUNSUPPORTED, "device %d beyond the no-allocation table", h->device);
   std::lock_guard<std::mutex> dev_lock(g_noalloc_mu[h->device]);
@@ -1224,10 +1369,12 @@ int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
   p.k_chunks = static_cast<int32_t>((h->ld + knn::kKChunk - 1) / knn::kKChunk);
   p.stages = static_cast<int32_t>(plan.stages);
   p.dataset_evict_first = plan.query_tiles == 1 ? 1 : 0;
+  p.metric = h->metric;
   KNN_CUDA(knn::launch_scan(qmap, h->xmap, p, plan, h->stream));
   KNN_CUDA(knn::launch_merge(part_d, part_i, k, plan.splits * k, static_cast<int>(plan.splits),
                              static_cast<int>(k), nq, h->row_offset, out_d, out_i, false,
-                             h->stream));
+                             h->stream, true, nullptr,
+                             h->metric == KNN_METRIC_INNER_PRODUCT));
   if (cd == 0)
     KNN_CUDA(cudaMemcpyAsync(distances, out_d, qk * 4, cudaMemcpyDeviceToHost, h->stream));
   if (cn == 0)

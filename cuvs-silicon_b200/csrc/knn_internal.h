@@ -6,6 +6,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "cuvs_b200.h"
+
 namespace knn {
 
 // Scan-kernel geometry (fixed for sm_100a).
@@ -42,6 +44,7 @@ struct ScanParams {
   int32_t k_chunks;  // ceil(ld / 64)
   int32_t stages;
   int32_t dataset_evict_first;
+  int32_t metric;  // KNN_METRIC_L2_EXPANDED or KNN_METRIC_INNER_PRODUCT
 };
 
 struct Plan {
@@ -111,10 +114,37 @@ inline int64_t exchange_words(int n_ranks, int64_t cap_qk) {
 // result into every rank's exchange buffer instead of out_d/out_i and raises
 // the query's flag there; mode 2 first waits (bounded) until every rank's
 // flag for the query has reached the epoch.
+// `negate_out` writes -d to out_d (the inner-product metric orders by -q.x
+// internally and reports q.x; padding becomes -inf).  Lists written to an
+// exchange buffer (mode 1) are never negated.
 cudaError_t launch_merge(const float* in_d, const uint32_t* in_i, int64_t stride_list,
                          int64_t stride_query, int n_lists, int k, int64_t n_queries,
                          int64_t index_offset, float* out_d, void* out_i, bool out_i64,
                          cudaStream_t stream, bool overlap = true,
-                         const Exchange* ex = nullptr);
+                         const Exchange* ex = nullptr, bool negate_out = false);
+
+// Exact fp32 re-ranking (knn_rerank.cu).  cand_{d,i}: per query the scan's
+// top kc (kc >= k, kc <= kMaxK) sorted candidates, local row indices,
+// scan distances in the internal order (minus the score for the inner
+// product).  rows: the fp32 rows (n x dim, dense).  Writes the k best by
+// exact fp32 distance to out_{d,i} (index_offset added; negate_out as in
+// launch_merge) and adds 1 to *uncertified for every query whose result is
+// not proven to be the exact fp32 top-k.  max_norm2: device scalar, the
+// largest fp32 norm |x16|^2 of the fp16 rows.
+cudaError_t launch_rerank(const float* queries, const float* rows, int64_t dim,
+                          const float* cand_d, const uint32_t* cand_i, int kc, int k,
+                          int64_t n_queries, int metric, const float* max_norm2,
+                          int64_t index_offset, float* out_d, void* out_i, bool out_i64,
+                          bool negate_out, int* uncertified, cudaStream_t stream);
+
+// out = the largest of norms[0..n) (norms >= 0).
+cudaError_t launch_max_norm(const float* norms, int64_t n, float* out, cudaStream_t stream);
+
+// Candidates the fp16 scan keeps per query for a re-ranked top-k: twice k,
+// at least 32 (the scan seeds its threshold for up to 32), at most kMaxK.
+inline int rerank_candidates(int64_t k) {
+  int64_t kc = 2 * k < 32 ? 32 : 2 * k;
+  return static_cast<int>(kc > kMaxK ? kMaxK : kc);
+}
 
 }  // namespace knn

@@ -143,8 +143,8 @@ __device__ __forceinline__ void get_entry(const List<E>& l, int e, float& d, uin
 
 template <typename OutIdx>
 __device__ __forceinline__ void store_out(float* out_d, OutIdx* out_i, int64_t at, float d,
-                                          uint32_t idx, int64_t index_offset) {
-  out_d[at] = d;
+                                          uint32_t idx, int64_t index_offset, float sign) {
+  out_d[at] = sign * d + 0.0f;  // + 0 maps -0 to +0
   if constexpr (sizeof(OutIdx) == 8) {
     out_i[at] = idx == kNoIndex ? OutIdx(-1) : static_cast<OutIdx>(idx) + index_offset;
   } else {
@@ -306,13 +306,13 @@ __device__ bool wait_for_peers(const Exchange& ex, int64_t q, int* s_abort) {
 template <typename OutIdx>
 __device__ void emit_result(const Exchange& ex, int64_t q, int k, const float* rd,
                             const uint32_t* ri, int count, int64_t index_offset, float* out_d,
-                            OutIdx* out_i) {
+                            OutIdx* out_i, float sign) {
   const float kInf = __int_as_float(0x7f800000);
   if (ex.mode != 1) {
     for (int e = threadIdx.x; e < k; e += blockDim.x) {
       const bool have = e < count;
       store_out(out_d, out_i, q * k + e, have ? rd[e] : kInf, have ? ri[e] : kNoIndex,
-                index_offset);
+                index_offset, sign);
     }
     return;
   }
@@ -343,7 +343,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
     merge_kernel(const float* __restrict__ in_d, const uint32_t* __restrict__ in_i,
                  int64_t stride_list, int64_t stride_query, int n_lists, int k,
                  int64_t index_offset, float* __restrict__ out_d, OutIdx* __restrict__ out_i,
-                 const Exchange ex) {
+                 const Exchange ex, float sign) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ uint8_t smem_raw[];
   float* sd = reinterpret_cast<float*>(smem_raw);
@@ -369,7 +369,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
   if (n_lists > kSelCap) {
     fold_merge<E>(sd, si, qd, qi, stride_list, n_lists, k, sd + kSelCap, si + kSelCap);
     __syncthreads();
-    emit_result(ex, q, k, sd + kSelCap, si + kSelCap, k, index_offset, out_d, out_i);
+    emit_result(ex, q, k, sd + kSelCap, si + kSelCap, k, index_offset, out_d, out_i, sign);
     return;
   }
   int p2 = 1;
@@ -460,14 +460,14 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
     __syncthreads();
     fold_merge<E>(sd, si, qd, qi, stride_list, n_lists, k, cd, ci);
     __syncthreads();
-    emit_result(ex, q, k, cd, ci, k, index_offset, out_d, out_i);
+    emit_result(ex, q, k, cd, ci, k, index_offset, out_d, out_i, sign);
     return;
   }
   if (count <= static_cast<int>(blockDim.x)) {
     // candidates are distinct (distinct row indices): rank counting places
     // the first k of them, sorted, in front of the selection array
     rank_place(cd, ci, count, seld, seli, k);
-    emit_result(ex, q, k, seld, seli, count, index_offset, out_d, out_i);
+    emit_result(ex, q, k, seld, seli, count, index_offset, out_d, out_i, sign);
     return;
   }
   int c2 = 1;
@@ -478,14 +478,14 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
   }
   __syncthreads();
   block_sort(cd, ci, c2);
-  emit_result(ex, q, k, cd, ci, count, index_offset, out_d, out_i);
+  emit_result(ex, q, k, cd, ci, count, index_offset, out_d, out_i, sign);
 }
 
 template <int E>
 cudaError_t launch_e(const float* in_d, const uint32_t* in_i, int64_t stride_list,
                      int64_t stride_query, int n_lists, int k, int64_t n_queries,
                      int64_t index_offset, float* out_d, void* out_i, bool out_i64,
-                     cudaStream_t stream, bool overlap, const Exchange& ex) {
+                     cudaStream_t stream, bool overlap, const Exchange& ex, float sign) {
   static_assert(kMergeWarps * 32 * E <= kStageEntries, "warp lists fit the staging area");
   static_assert(kCandCap <= kStageEntries, "candidates fit the staging area");
   constexpr size_t smem = static_cast<size_t>(kStageEntries) * 8;
@@ -525,11 +525,11 @@ cudaError_t launch_e(const float* in_d, const uint32_t* in_i, int64_t stride_lis
   if (out_i64) {
     return cudaLaunchKernelEx(&cfg, merge_kernel<E, int64_t>, in_d, in_i, stride_list,
                               stride_query, n_lists, k, index_offset, out_d,
-                              static_cast<int64_t*>(out_i), ex);
+                              static_cast<int64_t*>(out_i), ex, sign);
   }
   return cudaLaunchKernelEx(&cfg, merge_kernel<E, uint32_t>, in_d, in_i, stride_list,
                             stride_query, n_lists, k, index_offset, out_d,
-                            static_cast<uint32_t*>(out_i), ex);
+                            static_cast<uint32_t*>(out_i), ex, sign);
 }
 
 }  // namespace
@@ -537,23 +537,25 @@ cudaError_t launch_e(const float* in_d, const uint32_t* in_i, int64_t stride_lis
 cudaError_t launch_merge(const float* in_d, const uint32_t* in_i, int64_t stride_list,
                          int64_t stride_query, int n_lists, int k, int64_t n_queries,
                          int64_t index_offset, float* out_d, void* out_i, bool out_i64,
-                         cudaStream_t stream, bool overlap, const Exchange* ex_opt) {
+                         cudaStream_t stream, bool overlap, const Exchange* ex_opt,
+                         bool negate_out) {
   if (n_queries <= 0 || k <= 0) return cudaSuccess;
+  const float sign = negate_out ? -1.0f : 1.0f;
   Exchange none = {};
   const Exchange& ex = ex_opt ? *ex_opt : none;
   if (n_queries > 0x7fffffff) return cudaErrorInvalidValue;
   if (k <= 32)
     return launch_e<1>(in_d, in_i, stride_list, stride_query, n_lists, k, n_queries,
-                       index_offset, out_d, out_i, out_i64, stream, overlap, ex);
+                       index_offset, out_d, out_i, out_i64, stream, overlap, ex, sign);
   if (k <= 64)
     return launch_e<2>(in_d, in_i, stride_list, stride_query, n_lists, k, n_queries,
-                       index_offset, out_d, out_i, out_i64, stream, overlap, ex);
+                       index_offset, out_d, out_i, out_i64, stream, overlap, ex, sign);
   if (k <= 128)
     return launch_e<4>(in_d, in_i, stride_list, stride_query, n_lists, k, n_queries,
-                       index_offset, out_d, out_i, out_i64, stream, overlap, ex);
+                       index_offset, out_d, out_i, out_i64, stream, overlap, ex, sign);
   if (k <= 256)
     return launch_e<8>(in_d, in_i, stride_list, stride_query, n_lists, k, n_queries,
-                       index_offset, out_d, out_i, out_i64, stream, overlap, ex);
+                       index_offset, out_d, out_i, out_i64, stream, overlap, ex, sign);
   return cudaErrorInvalidValue;
 }
 

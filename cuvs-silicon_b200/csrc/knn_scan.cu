@@ -43,17 +43,35 @@ namespace knn {
 
 namespace {
 
-// A (distance, index) pair as one 64-bit key: distance bits above, index
-// below.  Distances here are >= 0 (clamped) or +inf, whose IEEE bit
-// patterns order like the values, so comparing keys as unsigned integers is
-// exactly the (distance, index) lexicographic order of src/cagra.cpp:233-238.
+// A (distance, index) pair as one 64-bit key: an order-preserving image of
+// the distance's bits above, the index below, so comparing keys as unsigned
+// integers is exactly the (distance, index) lexicographic order of
+// src/cagra.cpp:233-238.
+//   L2: distances are >= 0 (clamped, never -0) or +inf, whose IEEE bit
+//       patterns already order like the values: the image is the bits.
+//   Inner product (signed values): the image flips every bit of a negative
+//       float and only the sign bit of a non-negative one (-inf < ... < -0 <
+//       +0 < ... < +inf < NaN); the distance function never produces -0,
+//       so equal values have equal images.
+template <int kMetric>
 __device__ __forceinline__ uint64_t make_key(float d, uint32_t i) {
-  return (static_cast<uint64_t>(__float_as_uint(d)) << 32) | i;
+  uint32_t u = __float_as_uint(d);
+  if constexpr (kMetric == KNN_METRIC_INNER_PRODUCT) u ^= (u >> 31) ? 0xFFFFFFFFu : 0x80000000u;
+  return (static_cast<uint64_t>(u) << 32) | i;
 }
+template <int kMetric>
 __device__ __forceinline__ float key_dist(uint64_t key) {
-  return __uint_as_float(static_cast<uint32_t>(key >> 32));
+  uint32_t b = static_cast<uint32_t>(key >> 32);
+  if constexpr (kMetric == KNN_METRIC_INNER_PRODUCT) b ^= (b >> 31) ? 0x80000000u : 0xFFFFFFFFu;
+  return __uint_as_float(b);
 }
-constexpr uint64_t kEmptyKey = (static_cast<uint64_t>(0x7f800000u) << 32) | 0xFFFFFFFFull;
+// (+inf, no index)
+template <int kMetric>
+constexpr uint64_t empty_key() {
+  return (static_cast<uint64_t>(kMetric == KNN_METRIC_INNER_PRODUCT ? 0xFF800000u : 0x7f800000u)
+          << 32) |
+         0xFFFFFFFFull;
+}
 
 // Max-heap of keys stored column-wise: entry `pos` of query row `row` lives
 // at [pos * stride + row], so the 32 threads of a warp always touch 32
@@ -208,11 +226,29 @@ __device__ void mma_issuer(const ScanParams& p, const Smem& sm, uint32_t tmem_ba
   drain_wait(sm.drain, 0);
 }
 
-// Squared L2 from the fp32 dot product: |q|^2 + |x|^2 - 2 q.x, clamped at 0.
+// The distance the scan orders by, from the fp32 dot product, per metric.
 // Used by every pass over a tile so all passes see identical values.
-__device__ __forceinline__ float l2_from_dot(uint32_t acc_bits, float qn, float xn) {
-  const float d = fmaf(-2.0f, __uint_as_float(acc_bits), qn + xn);
-  return d <= 0.0f ? 0.0f : d;  // also maps -0 to +0 (key order); NaN stays NaN
+//   L2:            |q|^2 + |x|^2 - 2 q.x, clamped at 0 (squared L2); xn is
+//                  the row norm, +inf past the last row;
+//   inner product: xn - q.x with xn = 0 for a row and +inf past the last
+//                  row, so the ascending order is descending similarity
+//                  (the final merge negates it back) and 0 - q.x is never -0.
+// Both map -0 to +0 (key order); NaN stays NaN.
+template <int kMetric>
+__device__ __forceinline__ float dist_from_dot(uint32_t acc_bits, float qn, float xn) {
+  if constexpr (kMetric == KNN_METRIC_INNER_PRODUCT) {
+    return xn - __uint_as_float(acc_bits);
+  } else {
+    const float d = fmaf(-2.0f, __uint_as_float(acc_bits), qn + xn);
+    return d <= 0.0f ? 0.0f : d;
+  }
+}
+
+// Smallest float above a finite t (t is never -0 here).
+__device__ __forceinline__ float next_up(float t) {
+  const int b = __float_as_int(t);
+  if (t == 0.0f) return __int_as_float(1);
+  return __int_as_float(t > 0.0f ? b + 1 : b - 1);
 }
 
 // Ascending sort of 32 registers: bitonic network with every index a
@@ -251,6 +287,7 @@ struct RowState {
 // Moves every lane's buffered survivors into its heap.  Warp-uniform: all
 // lanes run the same number of iterations (the warp's largest buffer), so
 // the heap updates of the 32 query rows proceed in lock-step.
+template <int kMetric>
 __device__ __forceinline__ void flush_buffer(RowState& st, const Smem& sm, int k, int stride,
                                              int row) {
   const int maxc = __reduce_max_sync(0xffffffffu, st.cnt);
@@ -264,7 +301,7 @@ __device__ __forceinline__ void flush_buffer(RowState& st, const Smem& sm, int k
     }
   }
   st.cnt = 0;
-  st.thr = fminf(st.thr, key_dist(st.root));
+  st.thr = fminf(st.thr, key_dist<kMetric>(st.root));
 }
 
 // Epilogue warp.  Lane `row` owns query row `row` of the unit's query block.
@@ -280,6 +317,7 @@ __device__ __forceinline__ void flush_buffer(RowState& st, const Smem& sm, int k
 // t, has at least k rows of this unit at d <= t, so the unit's k-th best is
 // <= t and filtering with d <= t drops no result.  This keeps the first
 // tile from pushing all 256 columns through the heap.
+template <int kMetric>
 __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base, int warp,
                          int lane) {
   const int quad = warp & 3;              // TMEM lane quadrant this warp may access
@@ -298,22 +336,27 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
     const bool valid_q = warp_active && row < p.query_block && q < p.n_queries;
     const float qn = valid_q ? p.query_norms[q] : 0.0f;
     if (valid_q) {
-      for (int pos = 0; pos < k; ++pos) sm.heap[pos * stride + row] = kEmptyKey;
+      for (int pos = 0; pos < k; ++pos) sm.heap[pos * stride + row] = empty_key<kMetric>();
     }
     RowState st;
     st.thr = valid_q ? kInf : __int_as_float(0xff800000);
-    st.root = kEmptyKey;
+    st.root = empty_key<kMetric>();
     st.cnt = 0;
     // Row norms are prefetched one tile ahead into registers, then staged in
     // this warp's slice of shared memory so the chunk loop reads them with
-    // a shared-memory load instead of waiting on DRAM once per chunk.
+    // a shared-memory load instead of waiting on DRAM once per chunk (for
+    // the inner product: 0 for a row, +inf past the last row).
     float* const ns = sm.norm_stage + (warp - 2) * kAccCols;
     float nx[kAccCols / 32];
     auto prefetch_norms = [&](int64_t tile) {
 #pragma unroll
       for (int c = 0; c < kAccCols / 32; ++c) {
         const int64_t col = tile * kTileRows + c * 32 + lane;
-        nx[c] = col < p.n_rows ? __ldg(p.row_norms + col) : kInf;
+        if constexpr (kMetric == KNN_METRIC_INNER_PRODUCT) {
+          nx[c] = col < p.n_rows ? 0.0f : kInf;
+        } else {
+          nx[c] = col < p.n_rows ? __ldg(p.row_norms + col) : kInf;
+        }
       }
     };
     if (warp_active) prefetch_norms(t0);
@@ -346,10 +389,10 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
 #pragma unroll
             for (int j4 = 0; j4 < 8; ++j4) {
               const float4 v = n4[j4];  // same address in every lane: broadcast
-              g[4 * j4 + 0] = fminf(g[4 * j4 + 0], l2_from_dot(r[4 * j4 + 0], qn, v.x));
-              g[4 * j4 + 1] = fminf(g[4 * j4 + 1], l2_from_dot(r[4 * j4 + 1], qn, v.y));
-              g[4 * j4 + 2] = fminf(g[4 * j4 + 2], l2_from_dot(r[4 * j4 + 2], qn, v.z));
-              g[4 * j4 + 3] = fminf(g[4 * j4 + 3], l2_from_dot(r[4 * j4 + 3], qn, v.w));
+              g[4 * j4 + 0] = fminf(g[4 * j4 + 0], dist_from_dot<kMetric>(r[4 * j4 + 0], qn, v.x));
+              g[4 * j4 + 1] = fminf(g[4 * j4 + 1], dist_from_dot<kMetric>(r[4 * j4 + 1], qn, v.y));
+              g[4 * j4 + 2] = fminf(g[4 * j4 + 2], dist_from_dot<kMetric>(r[4 * j4 + 2], qn, v.z));
+              g[4 * j4 + 3] = fminf(g[4 * j4 + 3], dist_from_dot<kMetric>(r[4 * j4 + 3], qn, v.w));
             }
           }
           sort32(g);
@@ -358,8 +401,8 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
           float tk = g[0];
 #pragma unroll
           for (int j = 1; j < 32; ++j) tk = fmaxf(tk, j < k ? g[j] : 0.0f);
-          // keep d <= tk: the next float up (tk >= 0 here)
-          if (valid_q && tk < kInf) st.thr = fminf(st.thr, __int_as_float(__float_as_int(tk) + 1));
+          // keep d <= tk: the next float up
+          if (valid_q && tk < kInf) st.thr = fminf(st.thr, next_up(tk));
         }
         // One 32-column chunk: distances, threshold filter, survivor buffer.
         auto process_chunk = [&](const uint32_t (&r)[32], int c) {
@@ -368,10 +411,10 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
 #pragma unroll
           for (int j4 = 0; j4 < 8; ++j4) {
             const float4 v = n4[j4];  // row norms of columns 4*j4.., broadcast
-            dv[4 * j4 + 0] = l2_from_dot(r[4 * j4 + 0], qn, v.x);
-            dv[4 * j4 + 1] = l2_from_dot(r[4 * j4 + 1], qn, v.y);
-            dv[4 * j4 + 2] = l2_from_dot(r[4 * j4 + 2], qn, v.z);
-            dv[4 * j4 + 3] = l2_from_dot(r[4 * j4 + 3], qn, v.w);
+            dv[4 * j4 + 0] = dist_from_dot<kMetric>(r[4 * j4 + 0], qn, v.x);
+            dv[4 * j4 + 1] = dist_from_dot<kMetric>(r[4 * j4 + 1], qn, v.y);
+            dv[4 * j4 + 2] = dist_from_dot<kMetric>(r[4 * j4 + 2], qn, v.z);
+            dv[4 * j4 + 3] = dist_from_dot<kMetric>(r[4 * j4 + 3], qn, v.w);
           }
           const uint32_t col0 = static_cast<uint32_t>(t * kTileRows + c * 32);
 #pragma unroll
@@ -381,7 +424,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
             for (int j = 0; j < kRowBuf; ++j) mask |= (dv[h + j] < st.thr ? 1u : 0u) << j;
             if (__any_sync(0xffffffffu, mask != 0)) {
               if (__any_sync(0xffffffffu, st.cnt + __popc(mask) > kRowBuf)) {
-                flush_buffer(st, sm, k, stride, row);
+                flush_buffer<kMetric>(st, sm, k, stride, row);
                 mask = 0;
 #pragma unroll
                 for (int j = 0; j < kRowBuf; ++j) mask |= (dv[h + j] < st.thr ? 1u : 0u) << j;
@@ -389,7 +432,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
 #pragma unroll
               for (int j = 0; j < kRowBuf; ++j) {
                 if ((mask >> j) & 1u) {
-                  sm.buf[st.cnt * stride + row] = make_key(dv[h + j], col0 + h + j);
+                  sm.buf[st.cnt * stride + row] = make_key<kMetric>(dv[h + j], col0 + h + j);
                   ++st.cnt;
                 }
               }
@@ -418,10 +461,10 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
       ++tc;
       // survivors enter the heap at every tile end so thr tightens early (the
       // accumulator is already released; this overlaps the next tile's MMAs)
-      if (warp_active && __any_sync(0xffffffffu, st.cnt > 0)) flush_buffer(st, sm, k, stride, row);
+      if (warp_active && __any_sync(0xffffffffu, st.cnt > 0)) flush_buffer<kMetric>(st, sm, k, stride, row);
     }
     if (failed) break;
-    if (warp_active) flush_buffer(st, sm, k, stride, row);
+    if (warp_active) flush_buffer<kMetric>(st, sm, k, stride, row);
     if (valid_q) {
       // heap sort -> ascending (distance, index)
       for (int end = k - 1; end > 0; --end) {
@@ -435,13 +478,14 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
       uint32_t* oi = p.part_i + (static_cast<size_t>(q) * p.splits + s) * k;
       for (int r = 0; r < k; ++r) {
         const uint64_t key = sm.heap[r * stride + row];
-        od[r] = key_dist(key);
+        od[r] = key_dist<kMetric>(key);
         oi[r] = static_cast<uint32_t>(key);
       }
     }
   }
 }
 
+template <int kMetric>
 __global__ void __launch_bounds__(kScanThreads, 1)
     knn_scan_kernel(const __grid_constant__ CUtensorMap qmap,
                     const __grid_constant__ CUtensorMap xmap, const ScanParams p) {
@@ -485,7 +529,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) mma_issuer(p, sm, tmem_base);
   } else {
-    epilogue(p, sm, tmem_base, warp, lane);
+    epilogue<kMetric>(p, sm, tmem_base, warp, lane);
   }
 
   tc_fence_before();
@@ -577,8 +621,16 @@ cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap, const 
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  if (p.metric != KNN_METRIC_L2_EXPANDED && p.metric != KNN_METRIC_INNER_PRODUCT)
+    return cudaErrorInvalidValue;
+  const bool ip = p.metric == KNN_METRIC_INNER_PRODUCT;
   if (dev < 0 || dev >= 64 || !configured[dev]) {
-    e = cudaFuncSetAttribute(knn_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(knn_scan_kernel<KNN_METRIC_L2_EXPANDED>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemLimit));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(knn_scan_kernel<KNN_METRIC_INNER_PRODUCT>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemLimit));
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev] = true;
@@ -593,7 +645,8 @@ cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap, const 
   attr[0].val.programmaticStreamSerializationAllowed = overlap ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, knn_scan_kernel, qmap, xmap, p);
+  if (ip) return cudaLaunchKernelEx(&cfg, knn_scan_kernel<KNN_METRIC_INNER_PRODUCT>, qmap, xmap, p);
+  return cudaLaunchKernelEx(&cfg, knn_scan_kernel<KNN_METRIC_L2_EXPANDED>, qmap, xmap, p);
 }
 
 }  // namespace knn

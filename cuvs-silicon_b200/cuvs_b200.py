@@ -88,6 +88,9 @@ def lib() -> ctypes.CDLL:
                                        ctypes.POINTER(ctypes.c_double),
                                        ctypes.POINTER(I64), ctypes.POINTER(I64)]),
         "knn_index_reset_kernel_stats": (I, [P]),
+        "knn_index_set_rerank": (I, [P, I]),
+        "knn_index_rerank_stats": (I, [P, ctypes.POINTER(I64), ctypes.POINTER(I64)]),
+        "knn_index_search_noalloc": (I, [P, P, I64, I64, P, P]),
         "knn_selftest_bounded_wait": (I, [I, I64]),
         "knn_dispatch_count": (ctypes.c_uint64, []),
         "knn_reset_dispatch_count": (None, []),
@@ -267,6 +270,17 @@ class Index:
 
     def sync(self) -> None:
         _check(lib().knn_index_sync(self._h))
+
+    def set_rerank(self, on: bool) -> None:
+        """Exact fp32 re-ranking (call before build; see knn_index_set_rerank)."""
+        _check(lib().knn_index_set_rerank(self._h, 1 if on else 0))
+
+    def rerank_stats(self) -> dict:
+        """{'uncertified': queries of the last search not proven exact,
+        'widened': queries searched again with more candidates}."""
+        u, w = ctypes.c_int64(), ctypes.c_int64()
+        _check(lib().knn_index_rerank_stats(self._h, ctypes.byref(u), ctypes.byref(w)))
+        return {"uncertified": u.value, "widened": w.value}
 
     def set_peer_exchange(self, on: bool) -> None:
         _check(lib().knn_index_set_peer_exchange(self._h, 1 if on else 0))

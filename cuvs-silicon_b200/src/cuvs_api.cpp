@@ -53,8 +53,11 @@ std::atomic<std::uint64_t> g_manual_dispatches{0};
 
 // "CGRA" v1 container (src/cagra.cpp:268-276): magic, u32 version, i64 N,
 // i64 D, u32 graph degree, u32 flags (bit0 dataset, bit1 nav), then the
-// dataset (fp32), the graph (u32), and the navigation block.
+// dataset (fp32), the graph (u32), and the navigation block.  Flag bit 2
+// (unused by the reference, whose loader tests bits 0 and 1 only) marks a
+// brute-force index built for the InnerProduct metric.
 constexpr char kMagic[4] = {'C', 'G', 'R', 'A'};
+constexpr std::uint32_t kFlagInnerProduct = 4u;
 
 template <typename T>
 void put(std::ofstream& f, const T& v) {
@@ -297,8 +300,9 @@ index<float> build_impl(const raft::resources& res,
                         raft::device_matrix_view<const float, std::int64_t> rows,
                         std::int64_t row_offset, std::int64_t total_rows,
                         cuvs::distance::DistanceType metric) {
-  if (metric != cuvs::distance::DistanceType::L2Expanded)
-    throw std::invalid_argument("brute_force supports the L2Expanded metric");
+  if (metric != cuvs::distance::DistanceType::L2Expanded &&
+      metric != cuvs::distance::DistanceType::InnerProduct)
+    throw std::invalid_argument("brute_force supports the L2Expanded and InnerProduct metrics");
   if (rows.data_handle() == nullptr || rows.extent(0) <= 0 || rows.extent(1) <= 0)
     throw std::invalid_argument("brute_force build requires a non-empty dataset");
   knn_index* h = new_handle(res);
@@ -390,6 +394,7 @@ void serialize(const raft::resources& res, const std::string& path, const index<
   h.d = idx.dim();
   h.g = 0;
   h.flags = 1u;
+  if (idx.metric() == cuvs::distance::DistanceType::InnerProduct) h.flags |= kFlagInnerProduct;
   write_header(f, h);
   put_vec(f, rows.data(), rows.size());
   if (!f) throw std::runtime_error("serialize: write failed");
@@ -403,8 +408,10 @@ index<float> deserialize(const raft::resources& res, const std::string& path) {
   std::vector<float> rows;
   get_vec(f, rows, static_cast<std::size_t>(h.n * h.d));
   if (!f) throw std::runtime_error("deserialize: read failed");
-  return build(res, raft::make_device_matrix_view<const float, std::int64_t>(rows.data(), h.n,
-                                                                            h.d));
+  return build(res,
+               raft::make_device_matrix_view<const float, std::int64_t>(rows.data(), h.n, h.d),
+               (h.flags & kFlagInnerProduct) ? cuvs::distance::DistanceType::InnerProduct
+                                             : cuvs::distance::DistanceType::L2Expanded);
 }
 
 }  // namespace cuvs::neighbors::brute_force

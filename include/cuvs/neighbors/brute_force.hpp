@@ -76,7 +76,9 @@ index<float> build_shard(const raft::resources& res,
 
 // Exact k-NN, k = neighbors.extent(1).  int64 neighbours follow upstream
 // cuVS (missing neighbours are -1); uint32 neighbours follow the reference's
-// cagra contract (missing = UINT32_MAX).  Distances are squared L2.
+// cagra contract (missing = UINT32_MAX).  L2Expanded: distances are squared
+// L2, ascending.  InnerProduct: distances are the inner products q.x,
+// descending (largest first), ties by ascending index, missing = -inf.
 void search(const raft::resources& res, const search_params& params, const index<float>& idx,
             raft::device_matrix_view<const float, std::int64_t> queries,
             raft::device_matrix_view<std::int64_t, std::int64_t> neighbors,
@@ -93,7 +95,8 @@ void search(const raft::resources& res, const index<float>& idx,
 // Saves / loads an index in the reference's "CGRA" v1 container with graph
 // degree 0 and the dataset present (src/cagra.cpp:268-366); the rows are
 // written as fp32 (the fp16 device rows widen exactly) so the reference can
-// read the file, and loading rebuilds the device copy.
+// read the file, and loading rebuilds the device copy.  The metric travels
+// in flag bit 2 (set for InnerProduct).
 void serialize(const raft::resources& res, const std::string& path, const index<float>& idx);
 index<float> deserialize(const raft::resources& res, const std::string& path);
 

@@ -59,8 +59,12 @@ extern "C" {
 #define KNN_DTYPE_F32 0
 #define KNN_DTYPE_F16 1
 
+/* Metrics.  L2Expanded: squared L2 distances, ascending.  InnerProduct
+ * (declared by the reference at include/cuvs/distance/distance.hpp:5-8 and
+ * rejected by its cagra::build, src/cagra.cpp:26-28): the inner products
+ * q.x, descending, ties by ascending index, padding -inf. */
 #define KNN_METRIC_L2_EXPANDED 0 /* cuvs::distance::DistanceType::L2Expanded */
-#define KNN_METRIC_INNER_PRODUCT 1
+#define KNN_METRIC_INNER_PRODUCT 1 /* cuvs::distance::DistanceType::InnerProduct */
 
 /* Largest k one search accepts (per-CTA top-k state must fit in shared
  * memory next to a two-stage pipeline and a survivor buffer).  The reference's Metal kernel caps k
@@ -179,6 +183,32 @@ int knn_index_search_async(knn_index* index, const float* queries,
                            float* distances);
 /* Waits for the index's stream and reports device-side errors. */
 int knn_index_sync(knn_index* index);
+
+/* Exact fp32 re-ranking (no counterpart in the reference's Metal path; it
+ * makes searches return what the reference's portable exact search,
+ * src/cagra.cpp:211-252, returns for the same fp32 rows).
+ *
+ * enabled != 0 before knn_index_build keeps the fp32 rows on the device
+ * (n_rows x dim x 4 bytes next to the fp16 copy; fp32 input only).  Each
+ * search then keeps max(32, 2k) (at most KNN_MAX_K) fp16-scan candidates
+ * per query, recomputes their distances from the fp32 rows with the
+ * reference's arithmetic (sequential fp32 sum of (q[d] - x[d])^2, no fused
+ * multiply-add; inner product: sequential fp32 sum of q[d] * x[d]) and
+ * returns the k best by (distance, index).  Reported distances are
+ * bit-identical to the reference's.  A query is CERTIFIED when a rounding
+ * bound proves that no row outside its candidates can enter its top-k
+ * (then its result is exactly the reference's).  A blocking search on one
+ * device repeats itself once with KNN_MAX_K candidates when some query is
+ * not certified.  Returns KNN_EINVAL (and keeps re-ranking enabled for the
+ * next build) when the index already holds rows built without their fp32
+ * copy.  enabled = 0 frees the fp32 rows. */
+int knn_index_set_rerank(knn_index* index, int enabled);
+
+/* For the most recent re-ranked search that completed (a blocking search,
+ * or knn_index_sync after knn_index_search_async): the number of queries
+ * whose result is not certified, and the number that were not certified
+ * with the first candidate count (and so were searched again). */
+int knn_index_rerank_stats(knn_index* index, int64_t* uncertified, int64_t* widened);
 
 /* Plans a search without running it (pure host arithmetic).  num_sms <= 0
  * uses 148 (B200).  No counterpart in the reference. */

@@ -27,6 +27,16 @@
  * A thread-parallel entry point splits queries across POSIX threads; each
  * query is still computed exactly as above, so results do not depend on the
  * thread count.
+ *
+ * Inner product (oracle_ip_knn): the reference declares
+ * DistanceType::InnerProduct (include/cuvs/distance/distance.hpp:5-8) but
+ * rejects it at build (src/cagra.cpp:26-28), so no reference code computes
+ * it and this half of the oracle is PARITY UNPINNED against the reference.
+ * It restates the published cuVS definition: score = sum over dims, in
+ * order, of q[d] * x[d] in fp32; order by (score descending, index
+ * ascending), i.e. by (-score, index) with the same selection as above;
+ * padding UINT32_MAX / -inf.  Its known answers are integer-valued cases
+ * (exact in any precision) in the tests.
  */
 #include <math.h>
 #include <pthread.h>
@@ -59,18 +69,30 @@ static void sift_down(float* hd, uint32_t* hi, int64_t size, int64_t pos) {
   hi[pos] = i;
 }
 
-/* Exact search for one query.  heap_d / heap_i are scratch of length k. */
+#define ORACLE_METRIC_L2 0
+#define ORACLE_METRIC_IP 1
+
+/* Exact search for one query.  heap_d / heap_i are scratch of length k.
+ * The selection orders by (key, index) ascending, key = the squared L2
+ * distance, or minus the inner product. */
 static void search_one(const float* base, int64_t n, int64_t dim,
                        const float* query, int64_t k, uint32_t* out_idx,
-                       float* out_dist, float* heap_d, uint32_t* heap_i) {
+                       float* out_dist, float* heap_d, uint32_t* heap_i,
+                       int metric) {
   const int64_t take = k < n ? k : n;
   int64_t size = 0;
   for (int64_t v = 0; v < n; ++v) {
     const float* x = base + v * dim;
     float dist = 0.0f;
-    for (int64_t d = 0; d < dim; ++d) {
-      const float delta = query[d] - x[d];
-      dist += delta * delta;
+    if (metric == ORACLE_METRIC_IP) {
+      float dot = 0.0f;
+      for (int64_t d = 0; d < dim; ++d) dot += query[d] * x[d];
+      dist = -dot;
+    } else {
+      for (int64_t d = 0; d < dim; ++d) {
+        const float delta = query[d] - x[d];
+        dist += delta * delta;
+      }
     }
     const uint32_t idx = (uint32_t)v;
     if (size < take) {
@@ -103,10 +125,10 @@ static void search_one(const float* base, int64_t n, int64_t dim,
   }
   for (int64_t r = 0; r < k; ++r) {
     if (r < size) {
-      out_dist[r] = heap_d[r];
+      out_dist[r] = metric == ORACLE_METRIC_IP ? -heap_d[r] : heap_d[r];
       out_idx[r] = heap_i[r];
     } else {
-      out_dist[r] = INFINITY;
+      out_dist[r] = metric == ORACLE_METRIC_IP ? -INFINITY : INFINITY;
       out_idx[r] = ORACLE_NO_INDEX;
     }
   }
@@ -119,6 +141,7 @@ typedef struct {
   int64_t q_begin, q_end, k;
   uint32_t* out_idx;
   float* out_dist;
+  int metric;
   int status;
 } worker_arg;
 
@@ -135,7 +158,7 @@ static void* worker(void* p) {
   }
   for (int64_t q = a->q_begin; q < a->q_end; ++q) {
     search_one(a->base, a->n, a->dim, a->queries + q * a->dim, a->k,
-               a->out_idx + q * a->k, a->out_dist + q * a->k, hd, hi);
+               a->out_idx + q * a->k, a->out_dist + q * a->k, hd, hi, a->metric);
   }
   free(hd);
   free(hi);
@@ -148,9 +171,10 @@ static void* worker(void* p) {
  * base: n x dim, queries: nq x dim, outputs: nq x k.
  * Returns 0 on success, -1 on invalid arguments or allocation failure.
  */
-int oracle_l2_knn(const float* base, int64_t n, int64_t dim,
-                  const float* queries, int64_t nq, int64_t k,
-                  uint32_t* out_idx, float* out_dist, int n_threads) {
+static int knn_threads(const float* base, int64_t n, int64_t dim,
+                       const float* queries, int64_t nq, int64_t k,
+                       uint32_t* out_idx, float* out_dist, int n_threads,
+                       int metric) {
   if (n < 0 || dim <= 0 || nq < 0 || k < 0) return -1;
   if (nq == 0 || k == 0) return 0;
   if (!base || !queries || !out_idx || !out_dist) return -1;
@@ -174,6 +198,7 @@ int oracle_l2_knn(const float* base, int64_t n, int64_t dim,
     a->k = k;
     a->out_idx = out_idx;
     a->out_dist = out_dist;
+    a->metric = metric;
   }
   int rc = 0;
   if (n_threads == 1) {
@@ -194,6 +219,21 @@ int oracle_l2_knn(const float* base, int64_t n, int64_t dim,
   free(args);
   free(th);
   return rc;
+}
+
+int oracle_l2_knn(const float* base, int64_t n, int64_t dim,
+                  const float* queries, int64_t nq, int64_t k,
+                  uint32_t* out_idx, float* out_dist, int n_threads) {
+  return knn_threads(base, n, dim, queries, nq, k, out_idx, out_dist,
+                     n_threads, ORACLE_METRIC_L2);
+}
+
+/* Exact inner-product k-NN (largest q.x first); same layout as above. */
+int oracle_ip_knn(const float* base, int64_t n, int64_t dim,
+                  const float* queries, int64_t nq, int64_t k,
+                  uint32_t* out_idx, float* out_dist, int n_threads) {
+  return knn_threads(base, n, dim, queries, nq, k, out_idx, out_dist,
+                     n_threads, ORACLE_METRIC_IP);
 }
 
 /*

@@ -160,6 +160,8 @@ def port_lib() -> ctypes.CDLL:
         ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
         ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
         ctypes.c_int]
+    lib.oracle_ip_knn.restype = ctypes.c_int
+    lib.oracle_ip_knn.argtypes = lib.oracle_l2_knn.argtypes
     lib.oracle_merge_lists.restype = ctypes.c_int
     lib.oracle_merge_lists.argtypes = [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
@@ -193,18 +195,22 @@ def _c(a: np.ndarray, dtype) -> np.ndarray:
     return np.ascontiguousarray(a, dtype=dtype)
 
 
-def port_knn(base, queries, k, threads: int = 1):
-    """C restatement (oracle/knn_oracle.c).  Returns (idx uint32, dist f32)."""
+def port_knn(base, queries, k, threads: int = 1, metric: int = 0):
+    """C restatement (oracle/knn_oracle.c).  Returns (idx uint32, dist f32).
+
+    metric 0: squared L2, ascending.  metric 1: inner product, descending
+    (no reference counterpart: parity unpinned, see knn_oracle.c)."""
     base = _c(base, np.float32)
     queries = _c(queries, np.float32)
     n, dim = base.shape
     nq = queries.shape[0]
     idx = np.empty((nq, k), dtype=np.uint32)
     dist = np.empty((nq, k), dtype=np.float32)
-    rc = port_lib().oracle_l2_knn(base.ctypes.data, n, dim, queries.ctypes.data,
-                                  nq, k, idx.ctypes.data, dist.ctypes.data, threads)
+    fn = port_lib().oracle_ip_knn if metric == 1 else port_lib().oracle_l2_knn
+    rc = fn(base.ctypes.data, n, dim, queries.ctypes.data,
+            nq, k, idx.ctypes.data, dist.ctypes.data, threads)
     if rc != 0:
-        raise ValueError("oracle_l2_knn failed")
+        raise ValueError("oracle knn failed")
     return idx, dist
 
 
@@ -337,6 +343,12 @@ def exact_dist64(base16: np.ndarray, queries16: np.ndarray, idx: np.ndarray) -> 
 
 def check_parity(base16, queries16, got_i, got_d, ora_i, ora_d,
                  rel_tol: float = 1e-3, eps: float = 1e-6) -> Parity:
+    with np.errstate(invalid="ignore"):  # inf - inf of padding slots (masked)
+        return _check_parity(base16, queries16, got_i, got_d, ora_i, ora_d, rel_tol, eps)
+
+
+def _check_parity(base16, queries16, got_i, got_d, ora_i, ora_d,
+                  rel_tol: float, eps: float) -> Parity:
     """Acceptance rule of the fp16 engine against the oracle.
 
     * rank by rank, the index equals the oracle's, or the float64 distances of
@@ -396,6 +408,75 @@ def check_parity(base16, queries16, got_i, got_d, ora_i, ora_d,
     ok = (not tol_bad.any()) and recall == 1.0 and dist_ok and sorted_ok and padding_ok
     detail = (f"idx_mismatch={int(mism.sum())} tol_violation={int(tol_bad.sum())} "
               f"recall={recall:.6f} max_rel_dist_err={max_rel:.3e} dist_ok={dist_ok} "
+              f"sorted={sorted_ok} padding={padding_ok}")
+    return Parity(ok, int(mism.sum()), int(tol_bad.sum()), recall, max_rel,
+                  sorted_ok, padding_ok, detail)
+
+
+def check_parity_ip(base16, queries16, got_i, got_d, ora_i, ora_d,
+                    rel_tol: float = 1e-3) -> Parity:
+    with np.errstate(invalid="ignore"):  # inf - inf of padding slots (masked)
+        return _check_parity_ip(base16, queries16, got_i, got_d, ora_i, ora_d, rel_tol)
+
+
+def _check_parity_ip(base16, queries16, got_i, got_d, ora_i, ora_d,
+                     rel_tol: float) -> Parity:
+    """Acceptance rule for the inner-product metric (scores, largest first).
+
+    Scores are float64 dot products of the fp16-rounded vectors.  The error
+    scale of a score is s_q = |q| * max_x |x| (Cauchy-Schwarz bound of any
+    score of q), and:
+    * rank by rank, the index equals the oracle's, or the two scores differ
+      by at most rel_tol * s_q;
+    * recall@k = 1 where a returned row counts as a hit if its score is
+      >= the oracle's k-th score - rel_tol * s_q, and no index repeats;
+    * returned scores are within rel_tol * s_q of float64;
+    * output sorted descending; slots beyond n padded with UINT32_MAX / -inf.
+    """
+    got_i = np.asarray(got_i, dtype=np.uint32)
+    ora_i = np.asarray(ora_i, dtype=np.uint32)
+    got_d = np.asarray(got_d, dtype=np.float32)
+    nq, k = ora_i.shape
+    b64 = base16.astype(np.float64)
+    q64 = queries16.astype(np.float64)
+    xmax = float(np.sqrt((b64 * b64).sum(1)).max()) if len(b64) else 0.0
+    s_q = np.maximum(np.sqrt((q64 * q64).sum(1)) * xmax, 1e-30)
+
+    def scores(idx):
+        out = np.full(idx.shape, -np.inf)
+        for q in range(nq):
+            v = idx[q] != NO_INDEX
+            if v.any():
+                out[q, v] = b64[idx[q][v].astype(np.int64)] @ q64[q]
+        return out
+
+    S_o, S_g = scores(ora_i), scores(got_i)
+    pad_o, pad_g = ora_i == NO_INDEX, got_i == NO_INDEX
+    padding_ok = bool(np.array_equal(pad_o, pad_g)) and bool(
+        np.all(np.isneginf(got_d[pad_g])))
+    mism = (got_i != ora_i) & ~pad_o
+    both = ~pad_o & ~pad_g
+    tol = rel_tol * s_q[:, None]
+    tol_bad = (mism & both & (np.abs(S_g - S_o) > tol)) | (mism & (pad_o != pad_g))
+    hits = total = 0
+    for q in range(nq):
+        m = int((~pad_o[q]).sum())
+        if m == 0:
+            continue
+        kth = S_o[q][~pad_o[q]].min()
+        g = got_i[q][~pad_g[q]]
+        uniq = len(set(g.tolist())) == len(g)
+        h = int(np.sum(S_g[q][~pad_g[q]] >= kth - tol[q, 0])) if uniq else 0
+        hits += min(h, m)
+        total += m
+    recall = hits / total if total else 1.0
+    derr = np.where(both, np.abs(got_d.astype(np.float64) - np.where(both, S_g, 0.0)), 0.0)
+    dist_ok = bool(np.all(derr <= tol))
+    max_rel = float((derr / tol).max() * rel_tol) if both.any() else 0.0
+    sorted_ok = all(not np.any(np.diff(got_d[q][~pad_g[q]]) > 0) for q in range(nq))
+    ok = (not tol_bad.any()) and recall == 1.0 and dist_ok and sorted_ok and padding_ok
+    detail = (f"idx_mismatch={int(mism.sum())} tol_violation={int(tol_bad.sum())} "
+              f"recall={recall:.6f} max_score_err/s_q={max_rel:.3e} dist_ok={dist_ok} "
               f"sorted={sorted_ok} padding={padding_ok}")
     return Parity(ok, int(mism.sum()), int(tol_bad.sum()), recall, max_rel,
                   sorted_ok, padding_ok, detail)

@@ -257,9 +257,38 @@ static void test_save_load_and_brute_force(const std::string& tmpdir) {
   auto as_cagra = cg::load_index(bpath);
   EXPECT(as_cagra.rows() == n && as_cagra.dataset().size() == static_cast<std::size_t>(n * d));
 
+  // InnerProduct (rejected by cagra::build, src/cagra.cpp:26-28; accepted by
+  // brute_force): integer vectors, so the scores are exact.  Database rows
+  // (1,0) (0,1) (2,2) (-1,3), query (3,1): scores 3, 1, 8, 0 -> rows
+  // 2, 0, 1, 3, then padding (-1, -inf).
+  const std::vector<float> ipdb = {1, 0, 0, 1, 2, 2, -1, 3};
+  const std::vector<float> ipq = {3, 1};
+  auto ipi = bf::build(res, raft::make_device_matrix_view<const float, std::int64_t>(ipdb.data(), 4, 2),
+                       cuvs::distance::DistanceType::InnerProduct);
+  EXPECT(ipi.metric() == cuvs::distance::DistanceType::InnerProduct);
+  std::vector<std::int64_t> ipl(5);
+  std::vector<float> ips(5);
+  bf::search(res, ipi, raft::make_device_matrix_view<const float, std::int64_t>(ipq.data(), 1, 2),
+             raft::make_device_matrix_view<std::int64_t, std::int64_t>(ipl.data(), 1, 5),
+             raft::make_device_matrix_view<float, std::int64_t>(ips.data(), 1, 5));
+  EXPECT((ipl == std::vector<std::int64_t>{2, 0, 1, 3, -1}));
+  EXPECT(ips[0] == 8.0f && ips[1] == 3.0f && ips[2] == 1.0f && ips[3] == 0.0f &&
+         std::isinf(ips[4]) && ips[4] < 0);
+  // the metric survives serialisation (flag bit 2 of the container)
+  const std::string ippath = tmpdir + "/bf_ip_index.bin";
+  bf::serialize(res, ippath, ipi);
+  auto ipl2 = bf::deserialize(res, ippath);
+  EXPECT(ipl2.metric() == cuvs::distance::DistanceType::InnerProduct);
+  std::vector<std::int64_t> ipl3(5);
+  std::vector<float> ips3(5);
+  bf::search(res, ipl2, raft::make_device_matrix_view<const float, std::int64_t>(ipq.data(), 1, 2),
+             raft::make_device_matrix_view<std::int64_t, std::int64_t>(ipl3.data(), 1, 5),
+             raft::make_device_matrix_view<float, std::int64_t>(ips3.data(), 1, 5));
+  EXPECT(ipl3 == ipl && ips3 == ips);
+  cg::index_params ipp;
+  ipp.metric = cuvs::distance::DistanceType::InnerProduct;
   EXPECT(throws<std::invalid_argument>([&] {
-    bf::build(res, raft::make_device_matrix_view<const float, std::int64_t>(base.data(), n, d),
-              cuvs::distance::DistanceType::InnerProduct);
+    cg::build(res, ipp, raft::make_device_matrix_view<const float, std::int64_t>(base.data(), n, d));
   }));
 }
 
