@@ -21,6 +21,9 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 #include <dlfcn.h>
+#include <fcntl.h>
+#include <sys/stat.h>
+#include <unistd.h>
 #include <nccl.h>
 
 #include <algorithm>
@@ -902,6 +905,183 @@ int build_impl(knn_index* h, const void* rows, int dtype, int64_t n, int64_t dim
   return KNN_OK;
 }
 
+// Streams rows [r0, r1) of a dataset file into the index (see
+// knn_index_build_file).  The host reads chunk c + 1 into one pinned buffer
+// while the device copies chunk c out of the other (a pitched copy that
+// drops the fvecs record headers on the way) and converts it to fp16 rows
+// and norms; at most two chunks are ever held on the host.
+int build_file_impl(knn_index* h, const char* path, int format, int metric, int n_ranks,
+                    int rank) {
+  if (!h || !path) return fail(KNN_EINVAL, "null index or path");
+  if (format != KNN_FILE_FVECS && format != KNN_FILE_BIN_F32)
+    return fail(KNN_EINVAL, "unknown file format %d", format);
+  if (metric != KNN_METRIC_L2_EXPANDED && metric != KNN_METRIC_INNER_PRODUCT)
+    return fail(KNN_EINVAL, "metric %d is not L2Expanded (0) or InnerProduct (1)", metric);
+  if (n_ranks < 1 || rank < 0 || rank >= n_ranks)
+    return fail(KNN_EINVAL, "rank %d of %d", rank, n_ranks);
+  const int fd = ::open(path, O_RDONLY | O_CLOEXEC);
+  if (fd < 0) return fail(KNN_EINVAL, "cannot open %s: %s", path, std::strerror(errno));
+  struct FdCloser {
+    int fd;
+    ~FdCloser() { ::close(fd); }
+  } closer{fd};
+  struct stat sb;
+  if (::fstat(fd, &sb) != 0) return fail(KNN_EINVAL, "cannot stat %s", path);
+  const int64_t fsize = static_cast<int64_t>(sb.st_size);
+  auto pread_all = [&](void* dst, int64_t bytes, int64_t off) -> bool {
+    char* p = static_cast<char*>(dst);
+    while (bytes > 0) {
+      const ssize_t r = ::pread(fd, p, static_cast<size_t>(bytes), static_cast<off_t>(off));
+      if (r < 0 && errno == EINTR) continue;
+      if (r <= 0) return false;
+      p += r;
+      bytes -= r;
+      off += r;
+    }
+    return true;
+  };
+  // shape: rows, dim, record size and where row 0 starts
+  int64_t total = 0, dim = 0, rec = 0, base = 0, lead = 0;
+  if (format == KNN_FILE_FVECS) {
+    int32_t d0 = 0;
+    if (fsize < 4 || !pread_all(&d0, 4, 0) || d0 <= 0)
+      return fail(KNN_EINVAL, "%s: not an fvecs file (first row width %d)", path, (int)d0);
+    dim = d0;
+    rec = 4 + 4 * dim;
+    if (fsize % rec != 0)
+      return fail(KNN_EINVAL, "%s: %lld bytes is not a whole number of %lld-byte rows", path,
+                  (long long)fsize, (long long)rec);
+    total = fsize / rec;
+    lead = 4;
+  } else {
+    int32_t hdr[2] = {0, 0};
+    if (fsize < 8 || !pread_all(hdr, 8, 0) || hdr[0] <= 0 || hdr[1] <= 0)
+      return fail(KNN_EINVAL, "%s: not a .bin matrix (shape %d x %d)", path, (int)hdr[0],
+                  (int)hdr[1]);
+    total = hdr[0];
+    dim = hdr[1];
+    rec = 4 * dim;
+    base = 8;
+    if (fsize != base + total * rec)
+      return fail(KNN_EINVAL, "%s: %lld bytes, %lld expected for %lld x %lld", path,
+                  (long long)fsize, (long long)(base + total * rec), (long long)total,
+                  (long long)dim);
+  }
+  int64_t r0 = 0, r1 = 0;
+  {
+    const int64_t per = (total + n_ranks - 1) / n_ranks;
+    r0 = std::min<int64_t>(total, static_cast<int64_t>(rank) * per);
+    r1 = std::min<int64_t>(total, r0 + per);
+  }
+  const int64_t n = r1 - r0;
+  if (n <= 0) return fail(KNN_EINVAL, "%s: rank %d of %d holds no rows", path, rank, n_ranks);
+  if (total >= static_cast<int64_t>(KNN_NO_INDEX))
+    return fail(KNN_EUNSUPPORTED, "at most 2^32 - 2 rows (uint32 neighbour indices)");
+  if (n > (int64_t(1) << 31) - 256) return fail(KNN_EUNSUPPORTED, "at most 2^31 - 256 rows per device");
+  if (dim > (int64_t(1) << 20)) return fail(KNN_EUNSUPPORTED, "dim above 2^20");
+
+  std::lock_guard<std::mutex> lock(h->mu);
+  KNN_CUDA(cudaSetDevice(h->device));
+  if (h->data) cudaFree(h->data);
+  if (h->norms) cudaFree(h->norms);
+  if (h->rows32) cudaFree(h->rows32);
+  h->data = nullptr;
+  h->norms = nullptr;
+  h->rows32 = nullptr;
+  h->n = 0;
+  const int64_t ld = row_ld(dim);
+  KNN_CUDA(cudaMalloc(&h->data, static_cast<size_t>(n) * ld * 2));
+  KNN_CUDA(cudaMalloc(&h->norms, static_cast<size_t>(n) * 4));
+  if (h->rerank) KNN_CUDA(cudaMalloc(&h->rows32, static_cast<size_t>(n) * dim * 4));
+
+  const int64_t chunk = std::max<int64_t>(1, (int64_t(64) << 20) / rec);
+  const int64_t chunk_rows = std::min(chunk, n);
+  void* pinned[2] = {nullptr, nullptr};
+  DevBuf stage[2];
+  cudaEvent_t done[2] = {nullptr, nullptr};
+  int st = KNN_OK;
+  auto cleanup = [&]() {
+    for (int b = 0; b < 2; ++b) {
+      if (done[b]) {
+        cudaEventSynchronize(done[b]);
+        cudaEventDestroy(done[b]);
+      }
+      if (pinned[b]) cudaFreeHost(pinned[b]);
+      stage[b].release();
+    }
+  };
+  for (int b = 0; b < 2 && st == KNN_OK; ++b) {
+    if (cudaMallocHost(&pinned[b], static_cast<size_t>(chunk_rows * rec)) != cudaSuccess ||
+        cudaEventCreateWithFlags(&done[b], cudaEventDisableTiming) != cudaSuccess)
+      st = fail(KNN_ENOMEM, "pinned staging buffers");
+    else if (!h->rerank)
+      st = stage[b].ensure(static_cast<size_t>(chunk_rows) * dim * 4);
+  }
+  int c = 0;
+  for (int64_t a = 0; a < n && st == KNN_OK; a += chunk, ++c) {
+    const int b = c & 1;
+    const int64_t rr = std::min(chunk, n - a);
+    // the buffer's previous copy must have left it before it is refilled
+    if (cudaEventSynchronize(done[b]) != cudaSuccess) {
+      st = fail(KNN_ECUDA, "dataset upload: %s", cudaGetErrorString(cudaGetLastError()));
+      break;
+    }
+    char* raw = static_cast<char*>(pinned[b]);
+    if (!pread_all(raw, rr * rec, base + (r0 + a) * rec)) {
+      st = fail(KNN_EINVAL, "%s: read failed at row %lld", path, (long long)(r0 + a));
+      break;
+    }
+    if (format == KNN_FILE_FVECS) {
+      for (int64_t r = 0; r < rr; ++r) {
+        int32_t w;
+        std::memcpy(&w, raw + r * rec, 4);
+        if (w != dim) {
+          st = fail(KNN_EINVAL, "%s: row %lld has width %d, expected %lld", path,
+                    (long long)(r0 + a + r), (int)w, (long long)dim);
+          break;
+        }
+      }
+      if (st != KNN_OK) break;
+    }
+    float* dst = h->rerank ? h->rows32 + a * dim : stage[b].as<float>();
+    cudaError_t e = cudaMemcpy2DAsync(dst, static_cast<size_t>(dim) * 4, raw + lead,
+                                      static_cast<size_t>(rec), static_cast<size_t>(dim) * 4,
+                                      static_cast<size_t>(rr), cudaMemcpyHostToDevice, h->stream);
+    if (e == cudaSuccess)
+      e = knn::launch_convert_rows(dst, false, rr, rr, dim, h->data + a * ld, ld, h->norms + a,
+                                   h->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(done[b], h->stream);
+    if (e != cudaSuccess) st = fail(KNN_ECUDA, "dataset upload: %s", cudaGetErrorString(e));
+    g_dispatch.fetch_add(1);
+  }
+  if (st == KNN_OK && h->rerank) {
+    const cudaError_t e = knn::launch_max_norm(h->norms, n, h->max_norm2, h->stream);
+    if (e != cudaSuccess) st = fail(KNN_ECUDA, "max norm: %s", cudaGetErrorString(e));
+  }
+  if (st == KNN_OK && cudaStreamSynchronize(h->stream) != cudaSuccess)
+    st = fail(KNN_ECUDA, "dataset upload: %s", cudaGetErrorString(cudaGetLastError()));
+  cleanup();
+  if (st == KNN_OK) st = encode_rows(&h->xmap, h->data, n, ld, knn::kTileRows);
+  if (st != KNN_OK) {
+    cudaFree(h->data);
+    cudaFree(h->norms);
+    if (h->rows32) cudaFree(h->rows32);
+    h->data = nullptr;
+    h->norms = nullptr;
+    h->rows32 = nullptr;
+    return st;
+  }
+  ++h->generation;
+  drop_graphs(h);
+  h->n = n;
+  h->dim = dim;
+  h->ld = ld;
+  h->metric = metric;
+  h->row_offset = r0;
+  h->total_rows = total;
+  return KNN_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1003,6 +1183,11 @@ int knn_index_build(knn_index* h, const void* rows, int dtype, int64_t n, int64_
 int knn_index_build_shard(knn_index* h, const void* rows, int dtype, int64_t n, int64_t dim,
                           int metric, int64_t row_offset, int64_t total_rows) {
   return build_impl(h, rows, dtype, n, dim, metric, row_offset, total_rows);
+}
+
+int knn_index_build_file(knn_index* h, const char* path, int format, int metric, int n_ranks,
+                         int rank) {
+  return build_file_impl(h, path, format, metric, n_ranks, rank);
 }
 
 int knn_index_copy_rows(knn_index* h, void* out, int dtype) {

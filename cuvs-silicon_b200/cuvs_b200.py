@@ -39,6 +39,8 @@ DTYPE_F32 = 0
 DTYPE_F16 = 1
 METRIC_L2_EXPANDED = 0
 METRIC_INNER_PRODUCT = 1
+FILE_FVECS = 0
+FILE_BIN_F32 = 1
 NO_INDEX = 0xFFFFFFFF
 MAX_K = 256
 
@@ -89,6 +91,7 @@ def lib() -> ctypes.CDLL:
                                        ctypes.POINTER(I64), ctypes.POINTER(I64)]),
         "knn_index_reset_kernel_stats": (I, [P]),
         "knn_index_set_rerank": (I, [P, I]),
+        "knn_index_build_file": (I, [P, ctypes.c_char_p, I, I, I, I]),
         "knn_index_rerank_stats": (I, [P, ctypes.POINTER(I64), ctypes.POINTER(I64)]),
         "knn_index_search_noalloc": (I, [P, P, I64, I64, P, P]),
         "knn_selftest_bounded_wait": (I, [I, I64]),
@@ -233,6 +236,13 @@ class Index:
                                                row_offset, total))
         return self
 
+    def build_file(self, path: str, fmt: int = FILE_FVECS, metric: int = METRIC_L2_EXPANDED,
+                   n_ranks: int = 1, rank: int = 0) -> None:
+        """Streams a dataset file (FILE_FVECS or FILE_BIN_F32) into the index;
+        with n_ranks > 1 only this rank's row shard is read."""
+        _check(lib().knn_index_build_file(self._h, os.fsencode(path), fmt, metric,
+                                          n_ranks, rank))
+
     def attach_comm(self, unique_id: bytes, n_ranks: int, rank: int) -> None:
         buf = ctypes.create_string_buffer(bytes(unique_id), 128)
         _check(lib().knn_index_attach_comm(self._h, buf, n_ranks, rank))
@@ -301,3 +311,45 @@ class Index:
 
     def reset_kernel_stats(self) -> None:
         _check(lib().knn_index_reset_kernel_stats(self._h))
+
+
+# ------------------------------------------------------------ dataset files
+# numpy readers and writers of the formats knn_index_build_file streams and
+# the C++ loaders (include/cuvs_silicon/sift_loader.hpp) read.
+
+def write_fvecs(path: str, rows) -> None:
+    rows = np.ascontiguousarray(rows, dtype=np.float32)
+    rec = np.empty((rows.shape[0], rows.shape[1] + 1), dtype=np.float32)
+    rec[:, 0] = np.array([rows.shape[1]], dtype=np.int32).view(np.float32)[0]
+    rec[:, 1:] = rows
+    rec.tofile(path)
+
+
+def read_fvecs(path: str) -> np.ndarray:
+    raw = np.fromfile(path, dtype=np.int32)
+    if raw.size == 0:
+        return np.empty((0, 0), np.float32)
+    dim = int(raw[0])
+    if dim <= 0 or raw.size % (dim + 1):
+        raise ValueError(f"{path}: not an fvecs file")
+    rec = raw.reshape(-1, dim + 1)
+    if np.any(rec[:, 0] != dim):
+        raise ValueError(f"{path}: rows of different widths")
+    return rec[:, 1:].view(np.float32).copy()
+
+
+def write_bin(path: str, matrix) -> None:
+    m = np.ascontiguousarray(matrix)
+    if m.dtype not in (np.float32, np.int32):
+        raise ValueError("bin matrices hold float32 or int32")
+    with open(path, "wb") as f:
+        np.array(m.shape, dtype=np.int32).tofile(f)
+        m.tofile(f)
+
+
+def read_bin(path: str, dtype=np.float32) -> np.ndarray:
+    raw = np.fromfile(path, dtype=np.int32)
+    rows, cols = int(raw[0]), int(raw[1])
+    if rows < 0 or cols < 0 or raw.size != 2 + rows * cols:
+        raise ValueError(f"{path}: shape {rows} x {cols} does not match the file")
+    return raw[2:].view(dtype).reshape(rows, cols).copy()

@@ -124,6 +124,23 @@ int knn_index_build_shard(knn_index* index, const void* rows, int dtype,
                           int64_t n_rows, int64_t dim, int metric,
                           int64_t row_offset, int64_t total_rows);
 
+/* Dataset file formats for knn_index_build_file. */
+#define KNN_FILE_FVECS 0   /* per row: int32 dim, dim float32 (src/sift_loader.cpp:21-64) */
+#define KNN_FILE_BIN_F32 1 /* int32 rows, int32 cols, rows x cols float32
+                              (tests/test_cohere_wiki_validation.cpp:40-52) */
+
+/* Builds the index from a dataset file without holding it in host memory:
+ * the file is read in 64 MiB chunks into two pinned buffers, and each chunk
+ * is copied to the device and converted while the next one is read.  With
+ * n_ranks > 1 only this rank's row shard (knn_shard_range) is read and the
+ * index reports global row indices (as knn_index_build_shard).  Every fvecs
+ * record must have the width of the first; the file must end at a record
+ * boundary.  Replaces the reference's load-then-build sequence
+ * (load_fvecs / load_bin followed by cagra::build, which copies the whole
+ * fp32 dataset into the index). */
+int knn_index_build_file(knn_index* index, const char* path, int format, int metric,
+                         int n_ranks, int rank);
+
 int64_t knn_index_rows(const knn_index* index);
 int64_t knn_index_dim(const knn_index* index);
 
