@@ -11,6 +11,10 @@ torch.distributed.run).  Modes:
   gpu         one GPU per rank: row shards built with global offsets,
               NCCL communicator attached, every rank searches and receives
               the merged global result, checked against the oracle.
+  gpu-exact   one GPU per rank: exact fp32 re-ranking on every shard (the
+              merged result must equal the oracle on the unrounded rows
+              byte for byte) and the inner-product metric, through the
+              NVLink peer exchange and the NCCL all-gather.
 Exit code 0 = pass.
 """
 import datetime
@@ -113,6 +117,38 @@ def main():
                     print("rank 0 detected the missing peer list", flush=True)
                 torch.cuda.synchronize()
             dist.barrier()
+        dist.barrier()
+        dist.destroy_process_group()
+        return 0
+    if mode == "gpu-exact":
+        torch.cuda.set_device(rank)
+        obj = [E.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        with E.Index(rank) as idx:
+            idx.set_rerank(True)
+            idx.build(base[lo:hi], row_offset=lo, total_rows=n)
+            idx.attach_comm(obj[0], world, rank)
+            for peer in (True, False):
+                idx.set_peer_exchange(peer)
+                for k in (1, 10, 100):
+                    gi, gd = idx.search(queries, k)
+                    oi, od = O.port_knn(base, queries, k, threads=4)
+                    assert idx.rerank_stats()["uncertified"] == 0, f"rank {rank} k={k}"
+                    assert np.array_equal(gi, oi) and np.array_equal(gd, od), \
+                        f"rank {rank} k={k} peer={peer}"
+        # a communicator id serves one communicator: a new one for this index
+        obj = [E.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        with E.Index(rank) as idx:
+            idx.build(base[lo:hi], metric=E.METRIC_INNER_PRODUCT, row_offset=lo, total_rows=n)
+            idx.attach_comm(obj[0], world, rank)
+            for peer in (True, False):
+                idx.set_peer_exchange(peer)
+                for k in (10, 64):
+                    gi, gd = idx.search(queries, k)
+                    oi, od = O.port_knn(b16, q16, k, threads=4, metric=1)
+                    par = O.check_parity_ip(b16, q16, gi, gd, oi, od, 1e-3)
+                    assert par.ok, f"rank {rank} k={k} peer={peer}: {par.detail}"
         dist.barrier()
         dist.destroy_process_group()
         return 0

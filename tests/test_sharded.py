@@ -60,3 +60,13 @@ def test_gpu_two_ranks_nccl(engine):
     rc, out = _launch("gpu", 2, 600)
     assert rc == 0, out[-4000:]
     assert "detected the missing peer list" in out, out[-4000:]
+
+
+@pytest.mark.gpu
+def test_gpu_two_ranks_exact_rerank_and_inner_product(engine):
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    rc, out = _launch("gpu-exact", 2, 600)
+    assert rc == 0, out[-4000:]
