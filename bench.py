@@ -55,6 +55,10 @@ def parse():
     ap.add_argument("--k", type=int, default=10)
     ap.add_argument("--centres", type=int, default=10_000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--metric", default="l2", choices=["l2", "ip"],
+                    help="l2: squared L2 (the headline); ip: inner product")
+    ap.add_argument("--rerank", action="store_true",
+                    help="exact fp32 re-ranking of the fp16 scan's candidates")
     ap.add_argument("--no-graphs", action="store_true",
                     help="launch every search directly instead of replaying CUDA graphs")
     a = ap.parse_args()
@@ -64,7 +68,12 @@ def parse():
 
 def workload_name(a):
     head = (a.n, a.dim, a.q, a.k) == (1_000_000, 1024, 100, 10)
-    return ("headline " if head else "") + f"N={a.n} D={a.dim} Q={a.q} K={a.k}"
+    name = ("headline " if head else "") + f"N={a.n} D={a.dim} Q={a.q} K={a.k}"
+    if a.metric == "ip":
+        name += " InnerProduct"
+    if a.rerank:
+        name += " exact-fp32-rerank"
+    return name
 
 
 def peaks():
@@ -287,11 +296,16 @@ def run_engine(a):
     idx.set_stream(stream.cuda_stream)
     if a.no_graphs:
         idx.set_graphs(False)
-    idx.build(shard, row_offset=lo, total_rows=a.n)
+    if a.rerank:
+        idx.set_rerank(True)
+    metric = E.METRIC_INNER_PRODUCT if a.metric == "ip" else E.METRIC_L2_EXPANDED
+    idx.build(shard, metric=metric, row_offset=lo, total_rows=a.n)
     torch.cuda.synchronize()
     host_base16 = None
-    if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        host_base16 = shard.half().float().cpu().numpy()
+    if rank == 0 and world == 1 and not a.no_cpu_baseline and a.metric == "l2":
+        # the rows the engine's results are exact for: fp16-rounded, or the
+        # fp32 rows themselves with re-ranking
+        host_base16 = (shard if a.rerank else shard.half().float()).cpu().numpy()
     del shard
     if world > 1:
         obj = [E.comm_unique_id() if rank == 0 else None]
@@ -369,7 +383,7 @@ def run_engine(a):
     extra = {}
     if host_base16 is not None:
         threads = host_threads()
-        q16 = queries.half().float().cpu().numpy()
+        q16 = (queries if a.rerank else queries.half().float()).cpu().numpy()
         sample = max(1, min(a.q, 2 * threads))
         qps, secs, ref_i, ref_d, kind = cpu_reference_qps(host_base16, q16, a.k, sample, threads)
         cpu = {"value": qps, "unit": UNIT, "cores": min(threads, sample), "kind": kind,
@@ -407,8 +421,11 @@ def run_engine(a):
                     "generated on device with torch (seeds 11/12/13)",
             "config": {"workload": workload_name(a), "n_rows": a.n, "dim": a.dim,
                        "n_queries": a.q, "k": a.k,
-                       "parallelism": f"row-shard x{world}" + (" + NCCL all-gather"
-                                                               if world > 1 else ""),
+                       "metric": "InnerProduct" if a.metric == "ip" else "L2Expanded",
+                       "exact_fp32_rerank": bool(a.rerank),
+                       "parallelism": f"row-shard x{world}" + (
+                           " + NVLink peer exchange of the per-rank top-k lists"
+                           if world > 1 else ""),
                        "l2": f"inputs larger than L2 (dataset shard {shard_mb:.0f} MiB "
                              f"> 126 MiB), no flush"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

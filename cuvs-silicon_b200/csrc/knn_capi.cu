@@ -227,7 +227,7 @@ struct knn_index {
 
   // per-search scratch
   DevBuf q32, q16, qnorm, part_d, part_i, out_d, out_i, gather_send, gather_recv;
-  DevBuf cand_d, cand_i, rr_d, rr_i;
+  DevBuf cand_d, cand_i, rr_d, rr_i, pilot, thr;
   int* err_dev = nullptr;
   int* err_host = nullptr;  // pinned
 
@@ -539,15 +539,32 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
   p.stages = static_cast<int32_t>(plan.stages);
   p.dataset_evict_first = plan.query_tiles == 1 ? 1 : 0;
   p.metric = h->metric;
+  p.pilot = 0;
+  p.pilot_out = nullptr;
+  p.thr_init = nullptr;
   const bool neg = h->metric == KNN_METRIC_INNER_PRODUCT;
 
   if (prof) KNN_CUDA(cudaEventRecord((*prof)[0], h->stream));
   // with timing events between kernels, launch them plainly serialised
   const bool overlap = prof == nullptr;
+  int launches = 2;
+  if (ks >= knn::kPilotMinK) {
+    // large k: a pilot pass over one tile per unit bounds every query's k-th
+    // distance, and the main pass filters with that bound from its first tile
+    p.pilot = 1;
+    p.pilot_out = h->pilot.as<float>();
+    KNN_CUDA(knn::launch_scan(qmap, h->xmap, p, plan, h->stream, overlap));
+    KNN_CUDA(knn::launch_pilot_threshold(p.pilot_out, static_cast<int>(plan.splits),
+                                         static_cast<int>(ks), nq, h->thr.as<float>(),
+                                         h->stream));
+    p.pilot = 0;
+    p.pilot_out = nullptr;
+    p.thr_init = h->thr.as<float>();
+    launches += 2;
+  }
   KNN_CUDA(knn::launch_scan(qmap, h->xmap, p, plan, h->stream, overlap));
   if (prof) KNN_CUDA(cudaEventRecord((*prof)[1], h->stream));
 
-  int launches = 2;
   // the lists the final stage merges: the scan's per-unit lists, or one
   // re-ranked list per query
   const float* ld = p.part_d;
@@ -652,7 +669,8 @@ int search_pass(knn_index* h, const float* queries, int64_t nq, int64_t k, int64
   const int64_t nq_pad = knn::padded_query_rows(plan);
   DevBuf* bufs[] = {&h->q16,    &h->qnorm,       &h->part_d,      &h->part_i,
                     &h->q32,    &h->out_d,       &h->out_i,       &h->gather_send,
-                    &h->gather_recv, &h->cand_d, &h->cand_i, &h->rr_d, &h->rr_i};
+                    &h->gather_recv, &h->cand_d, &h->cand_i, &h->rr_d, &h->rr_i,
+                    &h->pilot, &h->thr};
   for (DevBuf* b : bufs) b->grew = false;
   if ((st = h->q16.ensure(static_cast<size_t>(nq_pad) * h->ld * 2)) != KNN_OK) return st;
   if ((st = h->qnorm.ensure(static_cast<size_t>(nq) * 4)) != KNN_OK) return st;
@@ -664,6 +682,11 @@ int search_pass(knn_index* h, const float* queries, int64_t nq, int64_t k, int64
   if (h->comm) {
     if ((st = h->gather_send.ensure(qk * 8)) != KNN_OK) return st;
     if ((st = h->gather_recv.ensure(qk * 8 * h->n_ranks)) != KNN_OK) return st;
+  }
+  if (ks >= knn::kPilotMinK) {
+    if ((st = h->pilot.ensure(static_cast<size_t>(nq) * plan.splits * 32 * 4)) != KNN_OK)
+      return st;
+    if ((st = h->thr.ensure(static_cast<size_t>(nq) * 4)) != KNN_OK) return st;
   }
   if (rerank) {
     const size_t qks = static_cast<size_t>(nq) * ks;
@@ -1149,7 +1172,7 @@ int knn_index_destroy(knn_index* h) {
   if (h->comm) nccl().CommDestroy(h->comm);
   for (DevBuf* b : {&h->q32, &h->q16, &h->qnorm, &h->part_d, &h->part_i, &h->out_d, &h->out_i,
                     &h->gather_send, &h->gather_recv, &h->cand_d, &h->cand_i, &h->rr_d,
-                    &h->rr_i})
+                    &h->rr_i, &h->pilot, &h->thr})
     b->release();
   if (h->data) cudaFree(h->data);
   if (h->norms) cudaFree(h->norms);
@@ -1555,6 +1578,9 @@ int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
   p.stages = static_cast<int32_t>(plan.stages);
   p.dataset_evict_first = plan.query_tiles == 1 ? 1 : 0;
   p.metric = h->metric;
+  p.pilot = 0;
+  p.pilot_out = nullptr;
+  p.thr_init = nullptr;
   KNN_CUDA(knn::launch_scan(qmap, h->xmap, p, plan, h->stream));
   KNN_CUDA(knn::launch_merge(part_d, part_i, k, plan.splits * k, static_cast<int>(plan.splits),
                              static_cast<int>(k), nq, h->row_offset, out_d, out_i, false,

@@ -45,7 +45,21 @@ struct ScanParams {
   int32_t stages;
   int32_t dataset_evict_first;
   int32_t metric;  // KNN_METRIC_L2_EXPANDED or KNN_METRIC_INNER_PRODUCT
+  // Pilot pass (pilot = 1): each unit scans only its first tile and writes
+  // its 32 sorted group minima per query to pilot_out[q][splits][32].
+  int32_t pilot;
+  float* pilot_out;
+  // Main pass: per-query starting threshold (nullptr: none).
+  const float* thr_init;
 };
+
+// k above which a search runs the pilot pass first (see knn_scan.cu).
+constexpr int kPilotMinK = 33;
+
+// Per-query starting thresholds from a pilot pass's group minima
+// (pilot_threshold_kernel in knn_scan.cu); thr: [n_queries].
+cudaError_t launch_pilot_threshold(const float* pilot, int splits, int k, int64_t n_queries,
+                                   float* thr, cudaStream_t stream);
 
 struct Plan {
   int64_t query_block, query_tiles, row_tiles, splits, units, grid, stages;

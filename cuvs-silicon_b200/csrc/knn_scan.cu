@@ -96,6 +96,19 @@ __device__ __forceinline__ void heap_sift_down(uint64_t* h, int size, int stride
   h[pos * stride + row] = key;
 }
 
+// Adds `key` at position pos (= the heap's current size) of a max-heap.
+__device__ __forceinline__ void heap_sift_up(uint64_t* h, int stride, int row, int pos,
+                                             uint64_t key) {
+  while (pos > 0) {
+    const int parent = (pos - 1) >> 1;
+    const uint64_t pk = h[parent * stride + row];
+    if (pk >= key) break;
+    h[pos * stride + row] = pk;
+    pos = parent;
+  }
+  h[pos * stride + row] = key;
+}
+
 struct Smem {
   uint8_t* stages;
   uint64_t* heap;  // [k][query_block] keys
@@ -135,6 +148,7 @@ __device__ __forceinline__ void unit_range(const ScanParams& p, int u, int& m, i
   const int s = u / p.query_tiles;
   t0 = static_cast<int64_t>(s) * p.row_tiles / p.splits;
   t1 = static_cast<int64_t>(s + 1) * p.row_tiles / p.splits;
+  if (p.pilot && t1 > t0 + 1) t1 = t0 + 1;  // the pilot pass reads one tile per unit
 }
 
 // Bounded wait used while unwinding after an error: ignores the error word,
@@ -280,13 +294,15 @@ __device__ __forceinline__ void sort32(float (&g)[32]) { bitonic_sort<2>(g); }
 // and the number of buffered survivors.
 struct RowState {
   float thr;     // candidates with d < thr are kept
-  uint64_t root; // heap root key (worst kept entry)
+  uint64_t root; // heap root key (worst kept entry) once the heap holds k, else empty
   int cnt;       // survivors waiting in the row's buffer
+  int size;      // entries in the heap (<= k)
 };
 
 // Moves every lane's buffered survivors into its heap.  Warp-uniform: all
 // lanes run the same number of iterations (the warp's largest buffer), so
-// the heap updates of the 32 query rows proceed in lock-step.
+// the heap updates of the 32 query rows proceed in lock-step.  The heap
+// grows by sift-up until it holds k entries, then replaces its root.
 template <int kMetric>
 __device__ __forceinline__ void flush_buffer(RowState& st, const Smem& sm, int k, int stride,
                                              int row) {
@@ -294,7 +310,10 @@ __device__ __forceinline__ void flush_buffer(RowState& st, const Smem& sm, int k
   for (int b = 0; b < maxc; ++b) {
     if (b < st.cnt) {
       const uint64_t key = sm.buf[b * stride + row];
-      if (key < st.root) {
+      if (st.size < k) {
+        heap_sift_up(sm.heap, stride, row, st.size, key);
+        if (++st.size == k) st.root = sm.heap[row];
+      } else if (key < st.root) {
         heap_sift_down(sm.heap, k, stride, row, 0, key);
         st.root = sm.heap[row];
       }
@@ -317,6 +336,10 @@ __device__ __forceinline__ void flush_buffer(RowState& st, const Smem& sm, int k
 // t, has at least k rows of this unit at d <= t, so the unit's k-th best is
 // <= t and filtering with d <= t drops no result.  This keeps the first
 // tile from pushing all 256 columns through the heap.
+// Pilot pass (p.pilot): only that first-tile pass runs, and each unit
+// writes its 32 sorted group minima to p.pilot_out for
+// pilot_threshold_kernel.  A main pass started with p.thr_init filters
+// every tile from the first one with that per-query threshold.
 template <int kMetric>
 __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base, int warp,
                          int lane) {
@@ -335,13 +358,11 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
     const int64_t q = static_cast<int64_t>(m) * p.query_block + row;
     const bool valid_q = warp_active && row < p.query_block && q < p.n_queries;
     const float qn = valid_q ? p.query_norms[q] : 0.0f;
-    if (valid_q) {
-      for (int pos = 0; pos < k; ++pos) sm.heap[pos * stride + row] = empty_key<kMetric>();
-    }
     RowState st;
-    st.thr = valid_q ? kInf : __int_as_float(0xff800000);
+    st.thr = valid_q ? (p.thr_init ? p.thr_init[q] : kInf) : __int_as_float(0xff800000);
     st.root = empty_key<kMetric>();
     st.cnt = 0;
+    st.size = 0;
     // Row norms are prefetched one tile ahead into registers, then staged in
     // this warp's slice of shared memory so the chunk loop reads them with
     // a shared-memory load instead of waiting on DRAM once per chunk (for
@@ -376,7 +397,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
         __syncwarp();
         if (t + 1 < t1) prefetch_norms(t + 1);
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + b * kAccCols;
-        if (t == t0 && k <= 32) {
+        if (t == t0 && (k <= 32 || p.pilot)) {
           float g[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) g[j] = kInf;
@@ -396,13 +417,23 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
             }
           }
           sort32(g);
-          // g is ascending, so g[k - 1] = max of g[0..k-1] (written without a
-          // run-time register index)
-          float tk = g[0];
+          if (p.pilot) {
+            if (valid_q) {
+              float4* o = reinterpret_cast<float4*>(
+                  p.pilot_out + (q * p.splits + u / p.query_tiles) * 32);
 #pragma unroll
-          for (int j = 1; j < 32; ++j) tk = fmaxf(tk, j < k ? g[j] : 0.0f);
-          // keep d <= tk: the next float up
-          if (valid_q && tk < kInf) st.thr = fminf(st.thr, next_up(tk));
+              for (int j4 = 0; j4 < 8; ++j4)
+                o[j4] = make_float4(g[4 * j4], g[4 * j4 + 1], g[4 * j4 + 2], g[4 * j4 + 3]);
+            }
+          } else {
+            // g is ascending, so g[k - 1] = max of g[0..k-1] (written without a
+            // run-time register index)
+            float tk = g[0];
+#pragma unroll
+            for (int j = 1; j < 32; ++j) tk = fmaxf(tk, j < k ? g[j] : 0.0f);
+            // keep d <= tk: the next float up
+            if (valid_q && tk < kInf) st.thr = fminf(st.thr, next_up(tk));
+          }
         }
         // One 32-column chunk: distances, threshold filter, survivor buffer.
         auto process_chunk = [&](const uint32_t (&r)[32], int c) {
@@ -442,17 +473,19 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
         // TMEM loads double-buffered: chunk c + 1 is in flight while chunk c
         // is processed.
         static_assert((kAccCols / 32) % 2 == 0, "chunk pairs");
-        uint32_t ra[32], rb[32];
-        tmem_ld_32x32b_x32(tbase, ra);
-        tmem_ld_wait_into(ra);
+        if (!p.pilot) {  // uniform over the grid: the warp stays converged
+          uint32_t ra[32], rb[32];
+          tmem_ld_32x32b_x32(tbase, ra);
+          tmem_ld_wait_into(ra);
 #pragma unroll 1
-        for (int c = 0; c < kAccCols / 32; c += 2) {
-          tmem_ld_32x32b_x32(tbase + (c + 1) * 32, rb);
-          process_chunk(ra, c);
-          tmem_ld_wait_into(rb);
-          if (c + 2 < kAccCols / 32) tmem_ld_32x32b_x32(tbase + (c + 2) * 32, ra);
-          process_chunk(rb, c + 1);
-          if (c + 2 < kAccCols / 32) tmem_ld_wait_into(ra);
+          for (int c = 0; c < kAccCols / 32; c += 2) {
+            tmem_ld_32x32b_x32(tbase + (c + 1) * 32, rb);
+            process_chunk(ra, c);
+            tmem_ld_wait_into(rb);
+            if (c + 2 < kAccCols / 32) tmem_ld_32x32b_x32(tbase + (c + 2) * 32, ra);
+            process_chunk(rb, c + 1);
+            if (c + 2 < kAccCols / 32) tmem_ld_wait_into(ra);
+          }
         }
       }
       tc_fence_before();
@@ -464,10 +497,13 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
       if (warp_active && __any_sync(0xffffffffu, st.cnt > 0)) flush_buffer<kMetric>(st, sm, k, stride, row);
     }
     if (failed) break;
+    if (p.pilot) continue;
     if (warp_active) flush_buffer<kMetric>(st, sm, k, stride, row);
     if (valid_q) {
-      // heap sort -> ascending (distance, index)
-      for (int end = k - 1; end > 0; --end) {
+      // heap sort of the st.size entries -> ascending (distance, index);
+      // the rest of the list is padding
+      const int n = st.size;
+      for (int end = n - 1; end > 0; --end) {
         const uint64_t top = sm.heap[row];
         const uint64_t last = sm.heap[end * stride + row];
         sm.heap[end * stride + row] = top;
@@ -477,7 +513,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
       float* od = p.part_d + (static_cast<size_t>(q) * p.splits + s) * k;
       uint32_t* oi = p.part_i + (static_cast<size_t>(q) * p.splits + s) * k;
       for (int r = 0; r < k; ++r) {
-        const uint64_t key = sm.heap[r * stride + row];
+        const uint64_t key = r < n ? sm.heap[r * stride + row] : empty_key<kMetric>();
         od[r] = key_dist<kMetric>(key);
         oi[r] = static_cast<uint32_t>(key);
       }
@@ -553,7 +589,62 @@ __global__ void bounded_wait_selftest_kernel(int* err, uint64_t limit_ns) {
   if (threadIdx.x == 0) mbar_wait(&bar, 0, err, kErrTimeoutFull, limit_ns);
 }
 
+// Per-query starting threshold from the pilot pass.  Each of the S units
+// left its 32 group minima sorted, every value the distance of a distinct
+// row.  With j = ceil(k / S) and r = ceil(k / j), tau = the r-th smallest of
+// the units' j-th values: r units each hold j values <= tau, so at least k
+// distinct rows lie at distance <= tau, and the k-th smallest distance of
+// the whole shard is <= tau.  Filtering with d <= tau (thr = the float
+// above tau) therefore keeps every row of the result.  When j > 32 or tau is
+// not finite the threshold is +inf (no filter).  One block per query.
+__global__ void __launch_bounds__(256)
+    pilot_threshold_kernel(const float* __restrict__ pilot, int splits, int k,
+                           float* __restrict__ thr) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int64_t q = blockIdx.x;
+  const float kInf = __int_as_float(0x7f800000);
+  const int j = (k + splits - 1) / splits;
+  if (j > 32) {
+    if (threadIdx.x == 0) thr[q] = kInf;
+    return;
+  }
+  const int r = (k + j - 1) / j;  // <= splits
+  extern __shared__ float sv[];   // [splits]
+  for (int s = threadIdx.x; s < splits; s += blockDim.x) {
+    const float v = pilot[(q * splits + s) * 32 + (j - 1)];
+    sv[s] = v == v ? v : kInf;  // NaN counts as +inf
+  }
+  __syncthreads();
+  // rank counting, ties broken by unit: exactly one unit has rank r - 1
+  for (int s = threadIdx.x; s < splits; s += blockDim.x) {
+    const float v = sv[s];
+    int rank = 0;
+    for (int t = 0; t < splits; ++t) {
+      const float w = sv[t];
+      rank += (w < v || (w == v && t < s)) ? 1 : 0;
+    }
+    if (rank == r - 1) thr[q] = v < kInf ? next_up(v) : kInf;
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_pilot_threshold(const float* pilot, int splits, int k, int64_t n_queries,
+                                   float* thr, cudaStream_t stream) {
+  if (n_queries <= 0) return cudaSuccess;
+  if (splits <= 0 || splits > 12288 || n_queries > 0x7fffffff) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(n_queries));
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = static_cast<size_t>(splits) * 4;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, pilot_threshold_kernel, pilot, splits, k, thr);
+}
 
 cudaError_t launch_bounded_wait_selftest(int* err, uint64_t limit_ns, cudaStream_t stream) {
   bounded_wait_selftest_kernel<<<1, 32, 0, stream>>>(err, limit_ns);
