@@ -54,7 +54,7 @@ struct ScanParams {
 };
 
 // k above which a search runs the pilot pass first (see knn_scan.cu).
-constexpr int kPilotMinK = 33;
+constexpr int kPilotMinK = 17;
 
 // Per-query starting thresholds from a pilot pass's group minima
 // (pilot_threshold_kernel in knn_scan.cu); thr: [n_queries].

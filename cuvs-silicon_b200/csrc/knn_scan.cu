@@ -67,7 +67,7 @@ __device__ __forceinline__ float key_dist(uint64_t key) {
 }
 // (+inf, no index)
 template <int kMetric>
-constexpr uint64_t empty_key() {
+__host__ __device__ constexpr uint64_t empty_key() {
   return (static_cast<uint64_t>(kMetric == KNN_METRIC_INNER_PRODUCT ? 0xFF800000u : 0x7f800000u)
           << 32) |
          0xFFFFFFFFull;
