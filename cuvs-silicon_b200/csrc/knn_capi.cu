@@ -227,7 +227,7 @@ struct knn_index {
 
   // per-search scratch
   DevBuf q32, q16, qnorm, part_d, part_i, out_d, out_i, gather_send, gather_recv;
-  DevBuf cand_d, cand_i, rr_d, rr_i, pilot, thr;
+  DevBuf cand_d, cand_i, rr_d, rr_i, pilot, thr, xdec;
   int* err_dev = nullptr;
   int* err_host = nullptr;  // pinned
 
@@ -606,8 +606,8 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
     launches += 1;
   } else if (h->peer_enabled && h->xcap > 0 && static_cast<int64_t>(qk) <= h->xcap) {
     // peer exchange: the local merge writes every query's list into every
-    // rank's exchange buffer over NVLink; the final merge waits for all of
-    // them (bounded) and merges from its own buffer
+    // rank's exchange buffer over NVLink as epoch-tagged words; the final
+    // merge collects them from its own buffer (bounded wait) and merges
     knn::Exchange ex = {};
     for (int r = 0; r < h->n_ranks; ++r) ex.base[r] = h->xpeer[r];
     ex.cap_qk = h->xcap;
@@ -620,10 +620,11 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
     KNN_CUDA(knn::launch_merge(ld, li, l_stride, q_stride, n_lists, static_cast<int>(k), nq, off,
                                nullptr, nullptr, false, h->stream, overlap, &ex));
     ex.mode = 2;
-    const float* rd = h->xbuf + static_cast<int64_t>(ex.parity) * h->n_ranks * 2 * h->xcap;
-    const uint32_t* ri = reinterpret_cast<const uint32_t*>(rd + h->xcap);
-    KNN_CUDA(knn::launch_merge(rd, ri, 2 * h->xcap, k, h->n_ranks, static_cast<int>(k), nq, 0,
-                               dst_d, dst_i, out_i64, h->stream, overlap, &ex, neg));
+    ex.dec_d = h->xdec.as<float>();
+    ex.dec_i = reinterpret_cast<uint32_t*>(ex.dec_d + qk * h->n_ranks);
+    KNN_CUDA(knn::launch_merge(ex.dec_d, ex.dec_i, k, static_cast<int64_t>(h->n_ranks) * k,
+                               h->n_ranks, static_cast<int>(k), nq, 0, dst_d, dst_i, out_i64,
+                               h->stream, overlap, &ex, neg));
     launches += 2;
   } else {
     // local merge into the send buffer: [dist k floats | idx k uint32] per query
@@ -670,7 +671,7 @@ int search_pass(knn_index* h, const float* queries, int64_t nq, int64_t k, int64
   DevBuf* bufs[] = {&h->q16,    &h->qnorm,       &h->part_d,      &h->part_i,
                     &h->q32,    &h->out_d,       &h->out_i,       &h->gather_send,
                     &h->gather_recv, &h->cand_d, &h->cand_i, &h->rr_d, &h->rr_i,
-                    &h->pilot, &h->thr};
+                    &h->pilot, &h->thr, &h->xdec};
   for (DevBuf* b : bufs) b->grew = false;
   if ((st = h->q16.ensure(static_cast<size_t>(nq_pad) * h->ld * 2)) != KNN_OK) return st;
   if ((st = h->qnorm.ensure(static_cast<size_t>(nq) * 4)) != KNN_OK) return st;
@@ -682,6 +683,7 @@ int search_pass(knn_index* h, const float* queries, int64_t nq, int64_t k, int64
   if (h->comm) {
     if ((st = h->gather_send.ensure(qk * 8)) != KNN_OK) return st;
     if ((st = h->gather_recv.ensure(qk * 8 * h->n_ranks)) != KNN_OK) return st;
+    if ((st = h->xdec.ensure(qk * 8 * h->n_ranks)) != KNN_OK) return st;
   }
   if (ks >= knn::kPilotMinK) {
     if ((st = h->pilot.ensure(static_cast<size_t>(nq) * plan.splits * 32 * 4)) != KNN_OK)
@@ -1172,7 +1174,7 @@ int knn_index_destroy(knn_index* h) {
   if (h->comm) nccl().CommDestroy(h->comm);
   for (DevBuf* b : {&h->q32, &h->q16, &h->qnorm, &h->part_d, &h->part_i, &h->out_d, &h->out_i,
                     &h->gather_send, &h->gather_recv, &h->cand_d, &h->cand_i, &h->rr_d,
-                    &h->rr_i, &h->pilot, &h->thr})
+                    &h->rr_i, &h->pilot, &h->thr, &h->xdec})
     b->release();
   if (h->data) cudaFree(h->data);
   if (h->norms) cudaFree(h->norms);

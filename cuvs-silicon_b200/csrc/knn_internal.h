@@ -96,28 +96,32 @@ inline int64_t padded_query_rows(const Plan& plan) {
 cudaError_t launch_bounded_wait_selftest(int* err, uint64_t limit_ns, cudaStream_t stream);
 
 // Peer exchange of per-rank top-k lists over NVLink (replaces the NCCL
-// all-gather for searches that fit).  Every rank owns one exchange buffer:
-//   data  [2 parities][n_ranks][2 * cap_qk words]: distances then indices of
-//         one rank's Q x k list (words of 4 bytes);
-//   flags [n_ranks][cap_qk] uint32: the search epoch whose list for query q
-//         from rank r has fully arrived.
+// all-gather for searches that fit).  Every rank owns one exchange buffer
+// of 16-byte entries [2 parities][n_ranks][cap_qk]: entry (p, r, q*k + e)
+// holds element e of rank r's list for query q as two 8-byte words, (epoch
+// << 32 | distance bits) and (epoch << 32 | row index).  An 8-byte store is
+// seen whole or not at all, so a reader that finds the search's epoch in
+// both words has the entry: no fence and no separate flag are needed.
 // `base[r]` is rank r's buffer as this GPU addresses it (its own allocation
-// or a CUDA IPC mapping).
+// or a CUDA IPC mapping).  Searches alternate parities, so a rank can write
+// search e + 1 while a slower peer still reads search e.
 constexpr int kMaxRanks = 8;
 struct Exchange {
   float* base[kMaxRanks];
   int64_t cap_qk;
   int n_ranks;
   int rank;
-  int mode;        // 0 none; 1 push this rank's lists to every rank; 2 wait for all ranks
-  uint32_t epoch;  // increases by one per search
-  int parity;      // epoch & 1: which data half this search uses
+  int mode;        // 0 none; 1 push this rank's lists to every rank; 2 receive and merge
+  uint32_t epoch;  // increases by one per search (never 0)
+  int parity;      // epoch & 1: which half this search uses
   int* err;        // device error word (wait timeouts)
+  float* dec_d;    // mode 2: received lists, decoded: [q][n_ranks][k]
+  uint32_t* dec_i;
 };
 constexpr int kErrTimeoutPeer = 7;  // a peer's list never arrived
 
 inline int64_t exchange_words(int n_ranks, int64_t cap_qk) {
-  return static_cast<int64_t>(n_ranks) * cap_qk * 5;  // 4 data words + 1 flag word
+  return static_cast<int64_t>(n_ranks) * cap_qk * 8;  // 2 parities x 16 bytes, in 4-byte words
 }
 
 // Merges n_lists sorted top-k lists per query into the final top-k.
@@ -125,9 +129,10 @@ inline int64_t exchange_words(int n_ranks, int64_t cap_qk) {
 // Valid indices get index_offset added.  out_i is uint32 (no-neighbour =
 // UINT32_MAX) or int64 (no-neighbour = -1) per out_i64.
 // `ex` (optional) selects the peer exchange: mode 1 writes each query's
-// result into every rank's exchange buffer instead of out_d/out_i and raises
-// the query's flag there; mode 2 first waits (bounded) until every rank's
-// flag for the query has reached the epoch.
+// result into every rank's exchange buffer instead of out_d/out_i; mode 2
+// receives every rank's list for the query from this rank's buffer (bounded
+// wait), decodes them to ex->dec_d/dec_i (which in_d/in_i must name, with
+// stride_list = k and stride_query = n_ranks * k) and merges them.
 // `negate_out` writes -d to out_d (the inner-product metric orders by -q.x
 // internally and reports q.x; padding becomes -inf).  Lists written to an
 // exchange buffer (mode 1) are never negated.

@@ -263,46 +263,60 @@ __device__ void fold_merge(float* sd, uint32_t* si, const float* qd, const uint3
   }
 }
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ void ld_relaxed_sys_v2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys_v2(uint64_t* p, uint64_t a, uint64_t b) {
+  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
 }
 
-// Mode 2: thread 0 waits (bounded, 1 s) until every rank's list for query q
-// carries this search's epoch.  Returns false (for the whole block) after
-// recording kErrTimeoutPeer when a list never arrives.
-__device__ bool wait_for_peers(const Exchange& ex, int64_t q, int* s_abort) {
-  if (threadIdx.x == 0) {
-    const uint32_t* flags = reinterpret_cast<const uint32_t*>(ex.base[ex.rank]) +
-                            static_cast<int64_t>(ex.n_ranks) * ex.cap_qk * 4;
-    int ok = 1;
+// Mode 2: the block collects every rank's list for query q from this
+// rank's exchange buffer, waiting (bounded, 1 s) until both words of each
+// entry carry this search's epoch, and decodes them to ex.dec_d/dec_i.
+// Returns false (for the whole block) after recording kErrTimeoutPeer when
+// an entry never arrives.
+__device__ bool receive_lists(const Exchange& ex, int64_t q, int k, int* s_abort) {
+  if (threadIdx.x == 0) *s_abort = 0;
+  __syncthreads();
+  const uint64_t* own = reinterpret_cast<const uint64_t*>(ex.base[ex.rank]);
+  const int total = ex.n_ranks * k;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int r = i / k;
+    const int e = i - r * k;
+    const uint64_t* src =
+        own + ((static_cast<int64_t>(ex.parity) * ex.n_ranks + r) * ex.cap_qk + q * k + e) * 2;
+    uint64_t a, b;
     uint64_t t0 = 0;
-    for (int r = 0; r < ex.n_ranks && ok; ++r) {
-      const uint32_t* f = flags + static_cast<int64_t>(r) * ex.cap_qk + q;
-      while (static_cast<int32_t>(ld_acquire_sys(f) - ex.epoch) < 0) {
-        uint64_t now;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-        if (t0 == 0) t0 = now;
-        if (now - t0 > 1000000000ull) {
-          atomicCAS(ex.err, 0, kErrTimeoutPeer);
-          ok = 0;
-          break;
-        }
+    bool ok = true;
+    while (true) {
+      ld_relaxed_sys_v2(src, a, b);
+      if (static_cast<uint32_t>(a >> 32) == ex.epoch && static_cast<uint32_t>(b >> 32) == ex.epoch)
+        break;
+      if (*reinterpret_cast<volatile int*>(s_abort)) {
+        ok = false;
+        break;
+      }
+      uint64_t now;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+      if (t0 == 0) t0 = now;
+      if (now - t0 > 1000000000ull) {
+        atomicCAS(ex.err, 0, kErrTimeoutPeer);
+        *reinterpret_cast<volatile int*>(s_abort) = 1;
+        ok = false;
+        break;
       }
     }
-    *s_abort = ok ? 0 : 1;
+    if (!ok) break;
+    ex.dec_d[q * total + i] = __uint_as_float(static_cast<uint32_t>(a));
+    ex.dec_i[q * total + i] = static_cast<uint32_t>(b);
   }
   __syncthreads();
-  return *s_abort == 0;
+  return *reinterpret_cast<volatile int*>(s_abort) == 0;
 }
 
 // Writes the query's first k result entries (the first `count` valid, the
 // rest padding) to the output, or in mode 1 to every rank's exchange buffer
-// followed by the query's flag there.  Called by every thread of the block.
+// as epoch-tagged words.  Called by every thread of the block.
 template <typename OutIdx>
 __device__ void emit_result(const Exchange& ex, int64_t q, int k, const float* rd,
                             const uint32_t* ri, int count, int64_t index_offset, float* out_d,
@@ -316,43 +330,34 @@ __device__ void emit_result(const Exchange& ex, int64_t q, int k, const float* r
     }
     return;
   }
-  const int64_t slot = 2 * ex.cap_qk;
-  for (int r = 0; r < ex.n_ranks; ++r) {
-    float* dst = ex.base[r] + (static_cast<int64_t>(ex.parity) * ex.n_ranks + ex.rank) * slot;
-    uint32_t* dsti = reinterpret_cast<uint32_t*>(dst + ex.cap_qk);
-    for (int e = threadIdx.x; e < k; e += blockDim.x) {
-      const bool have = e < count;
-      const uint32_t idx = have ? ri[e] : kNoIndex;
-      dst[q * k + e] = have ? rd[e] : kInf;
-      dsti[q * k + e] = idx == kNoIndex ? kNoIndex : static_cast<uint32_t>(idx + index_offset);
-    }
-  }
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int r = 0; r < ex.n_ranks; ++r) {
-      uint32_t* flags = reinterpret_cast<uint32_t*>(ex.base[r]) +
-                        static_cast<int64_t>(ex.n_ranks) * ex.cap_qk * 4;
-      st_release_sys(flags + static_cast<int64_t>(ex.rank) * ex.cap_qk + q, ex.epoch);
-    }
+  const uint64_t tag = static_cast<uint64_t>(ex.epoch) << 32;
+  const int64_t at = ((static_cast<int64_t>(ex.parity) * ex.n_ranks + ex.rank) * ex.cap_qk + q * k);
+  for (int e = threadIdx.x; e < k; e += blockDim.x) {
+    const bool have = e < count;
+    const uint32_t idx = have ? ri[e] : kNoIndex;
+    const uint32_t gidx = idx == kNoIndex ? kNoIndex : static_cast<uint32_t>(idx + index_offset);
+    const uint64_t wd = tag | __float_as_uint(have ? rd[e] : kInf);
+    const uint64_t wi = tag | gidx;
+    for (int r = 0; r < ex.n_ranks; ++r)
+      st_relaxed_sys_v2(reinterpret_cast<uint64_t*>(ex.base[r]) + (at + e) * 2, wd, wi);
   }
 }
 
+// Merges the lists of query blockIdx.x (every thread of the block).
 template <int E, typename OutIdx>
-__global__ void __launch_bounds__(kMergeWarps * 32)
-    merge_kernel(const float* __restrict__ in_d, const uint32_t* __restrict__ in_i,
-                 int64_t stride_list, int64_t stride_query, int n_lists, int k,
-                 int64_t index_offset, float* __restrict__ out_d, OutIdx* __restrict__ out_i,
-                 const Exchange ex, float sign) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+__device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
+                                            const uint32_t* __restrict__ in_i,
+                                            int64_t stride_list, int64_t stride_query,
+                                            int n_lists, int k, int64_t index_offset,
+                                            float* __restrict__ out_d,
+                                            OutIdx* __restrict__ out_i, const Exchange& ex,
+                                            float sign) {
   extern __shared__ uint8_t smem_raw[];
   float* sd = reinterpret_cast<float*>(smem_raw);
   uint32_t* si = reinterpret_cast<uint32_t*>(sd + kStageEntries);
   __shared__ int s_count;
-  __shared__ int s_abort;
 
   const int64_t q = blockIdx.x;
-  if (ex.mode == 2 && !wait_for_peers(ex, q, &s_abort)) return;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const float* qd = in_d + q * stride_query;
@@ -479,6 +484,33 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
   __syncthreads();
   block_sort(cd, ci, c2);
   emit_result(ex, q, k, cd, ci, count, index_offset, out_d, out_i, sign);
+}
+
+template <int E, typename OutIdx>
+__global__ void __launch_bounds__(kMergeWarps * 32)
+    merge_kernel(const float* __restrict__ in_d, const uint32_t* __restrict__ in_i,
+                 int64_t stride_list, int64_t stride_query, int n_lists, int k,
+                 int64_t index_offset, float* __restrict__ out_d, OutIdx* __restrict__ out_i,
+                 const __grid_constant__ Exchange ex, float sign) {
+  // The next kernel may be scheduled now; it waits for this one to finish
+  // before it reads anything this kernel writes.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  __shared__ int s_abort;
+  const int64_t q = blockIdx.x;
+  if (ex.mode == 2) {
+    // The input arrives through this rank's exchange buffer, tagged with the
+    // search's epoch, so the block starts without waiting for the local
+    // merge before it.  It waits at its end instead: this kernel then
+    // completes only after that one, as stream order requires.
+    if (receive_lists(ex, q, k, &s_abort))
+      merge_query<E, OutIdx>(in_d, in_i, stride_list, stride_query, n_lists, k, index_offset,
+                             out_d, out_i, ex, sign);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    return;
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  merge_query<E, OutIdx>(in_d, in_i, stride_list, stride_query, n_lists, k, index_offset, out_d,
+                         out_i, ex, sign);
 }
 
 template <int E>

@@ -38,8 +38,11 @@ template <bool kHalfIn>
 __global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, int64_t rows_out,
                                     int64_t dim, __half* __restrict__ out, int64_t ld,
                                     float* __restrict__ norms, bool vec) {
-  // launched as a programmatic dependent of the previous search's kernels,
-  // which may still read `out`: wait for them before writing
+  // Let the next kernel (the scan) be scheduled now: its dataset loads do
+  // not depend on this kernel, and it waits before reading the queries.
+  // This kernel is itself a programmatic dependent of the previous search's
+  // kernels, which may still read `out`: wait for them before writing.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane = threadIdx.x & 31;
   const int64_t warps_per_block = blockDim.x >> 5;

@@ -132,6 +132,7 @@ __global__ void __launch_bounds__(kRerankThreads)
                   const float* __restrict__ max_norm2, int64_t index_offset,
                   float* __restrict__ out_d, OutIdx* __restrict__ out_i, float sign,
                   int* __restrict__ uncertified) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ float s_d[kRerankThreads];
   __shared__ uint32_t s_i[kRerankThreads];

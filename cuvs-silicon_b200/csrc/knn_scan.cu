@@ -160,10 +160,35 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// TMA producer.  The kernel is launched as a programmatic dependent of the
+// query conversion, so it may start before that kernel's writes are
+// visible.  The dataset rows are not written while a search runs (a build
+// synchronises before it returns), so the dataset slabs of the first
+// stages are requested before griddepcontrol.wait and only the query slabs
+// wait for it: the first tile's load overlaps the kernels before this one.
 __device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap, const ScanParams& p,
                          const Smem& sm) {
   const uint64_t pol_q = policy_evict_last();
   const uint64_t pol_x = p.dataset_evict_first ? policy_evict_first() : policy_evict_normal();
+  // phase 1: dataset slabs of the first p.stages loads (every stage is free)
+  uint32_t pre = 0;
+  for (int u = blockIdx.x; u < p.units && pre < static_cast<uint32_t>(p.stages);
+       u += gridDim.x) {
+    int m;
+    int64_t t0, t1;
+    unit_range(p, u, m, t0, t1);
+    for (int64_t t = t0; t < t1 && pre < static_cast<uint32_t>(p.stages); ++t) {
+      const int32_t xy = static_cast<int32_t>(t * kTileRows);
+      for (int kc = 0; kc < p.k_chunks && pre < static_cast<uint32_t>(p.stages); ++kc) {
+        uint8_t* st = sm.stages + static_cast<size_t>(pre) * kStageBytes;
+        mbar_arrive_expect_tx(&sm.full[pre], kStageBytes);
+        tma_load_2d(st + kStageA, xmap, &sm.full[pre], kc * kKChunk, xy, pol_x);
+        ++pre;
+      }
+    }
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // phase 2: every load in order; the first `pre` only need their query slab
   uint32_t it = 0;
   bool failed = false;
   for (int u = blockIdx.x; u < p.units && !failed; u += gridDim.x) {
@@ -175,12 +200,17 @@ __device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap, const
       const int32_t xy = static_cast<int32_t>(t * kTileRows);
       for (int kc = 0; kc < p.k_chunks; ++kc) {
         const uint32_t slot = it % p.stages;
+        uint8_t* st = sm.stages + static_cast<size_t>(slot) * kStageBytes;
+        if (it < pre) {
+          tma_load_2d(st, qmap, &sm.full[slot], kc * kKChunk, qy, pol_q);
+          ++it;
+          continue;
+        }
         const uint32_t ph = (it / p.stages) & 1u;
         if (!mbar_wait(&sm.empty[slot], ph ^ 1u, p.err, kErrTimeoutEmpty)) {
           failed = true;
           break;
         }
-        uint8_t* st = sm.stages + static_cast<size_t>(slot) * kStageBytes;
         mbar_arrive_expect_tx(&sm.full[slot], kStageBytes);
         tma_load_2d(st, qmap, &sm.full[slot], kc * kKChunk, qy, pol_q);
         tma_load_2d(st + kStageA, xmap, &sm.full[slot], kc * kKChunk, xy, pol_x);
@@ -555,9 +585,11 @@ __global__ void __launch_bounds__(kScanThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *sm.tmem_slot;
   // Launched as a programmatic dependent: the set-up above overlaps the tail
-  // of the kernel before (the query conversion); wait for its results here,
-  // and let the merge kernel after this one be scheduled early.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // of the kernel before (the query conversion).  Every role but the
+  // producer waits for its results here (the producer waits itself, after
+  // requesting its first dataset slabs); the merge kernel after this one
+  // may be scheduled early.
+  if (warp != 0) asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
@@ -600,6 +632,7 @@ __global__ void bounded_wait_selftest_kernel(int* err, uint64_t limit_ns) {
 __global__ void __launch_bounds__(256)
     pilot_threshold_kernel(const float* __restrict__ pilot, int splits, int k,
                            float* __restrict__ thr) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int64_t q = blockIdx.x;
   const float kInf = __int_as_float(0x7f800000);
