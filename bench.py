@@ -39,7 +39,7 @@ PKG = os.path.join(ROOT, "cuvs-silicon_b200")
 
 METRIC = "QPS at N=1M D=1024 K=10 Q=100 (1/2/4/8 B200) and % of HBM/tensor roofline"
 UNIT = "queries/s"
-PUBLISHED_QPS = 1012.0  # reference README.md:23-27, Apple M3 Max
+PUBLISHED_QPS = 1012.0  # the reference README.md:23-27: Apple M3 Max, 1M x 1024, batch of 100
 L2_BYTES = 126 * 1024 * 1024
 
 
