@@ -227,7 +227,7 @@ struct knn_index {
 
   // per-search scratch
   DevBuf q32, q16, qnorm, part_d, part_i, out_d, out_i, gather_send, gather_recv;
-  DevBuf cand_d, cand_i, rr_d, rr_i, pilot, thr, xdec;
+  DevBuf cand_d, cand_i, rr_d, rr_i, pilot, thr, xdec, bound;
   int* err_dev = nullptr;
   int* err_host = nullptr;  // pinned
 
@@ -516,7 +516,8 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
   const int64_t nq_pad = knn::padded_query_rows(plan);
   if (rerank) KNN_CUDA(cudaMemsetAsync(h->uncert_dev, 0, sizeof(int), h->stream));
   KNN_CUDA(knn::launch_convert_rows(qsrc, false, nq, nq_pad, h->dim, h->q16.as<__half>(),
-                                    h->ld, h->qnorm.as<float>(), h->stream));
+                                    h->ld, h->qnorm.as<float>(), h->stream,
+                                    h->bound.as<uint32_t>(), nq));
   CUtensorMap qmap;
   if ((st = encode_rows(&qmap, h->q16.as<__half>(), nq_pad, h->ld, knn::kQueryRows)) != KNN_OK)
     return st;
@@ -542,6 +543,7 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
   p.pilot = 0;
   p.pilot_out = nullptr;
   p.thr_init = nullptr;
+  p.bound = nullptr;
   const bool neg = h->metric == KNN_METRIC_INNER_PRODUCT;
 
   if (prof) KNN_CUDA(cudaEventRecord((*prof)[0], h->stream));
@@ -562,6 +564,7 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
     p.thr_init = h->thr.as<float>();
     launches += 2;
   }
+  p.bound = h->bound.as<uint32_t>();
   KNN_CUDA(knn::launch_scan(qmap, h->xmap, p, plan, h->stream, overlap));
   if (prof) KNN_CUDA(cudaEventRecord((*prof)[1], h->stream));
 
@@ -671,10 +674,11 @@ int search_pass(knn_index* h, const float* queries, int64_t nq, int64_t k, int64
   DevBuf* bufs[] = {&h->q16,    &h->qnorm,       &h->part_d,      &h->part_i,
                     &h->q32,    &h->out_d,       &h->out_i,       &h->gather_send,
                     &h->gather_recv, &h->cand_d, &h->cand_i, &h->rr_d, &h->rr_i,
-                    &h->pilot, &h->thr, &h->xdec};
+                    &h->pilot, &h->thr, &h->xdec, &h->bound};
   for (DevBuf* b : bufs) b->grew = false;
   if ((st = h->q16.ensure(static_cast<size_t>(nq_pad) * h->ld * 2)) != KNN_OK) return st;
   if ((st = h->qnorm.ensure(static_cast<size_t>(nq) * 4)) != KNN_OK) return st;
+  if ((st = h->bound.ensure(static_cast<size_t>(nq) * 4)) != KNN_OK) return st;
   if ((st = h->part_d.ensure(static_cast<size_t>(plan.partial_bytes / 2))) != KNN_OK) return st;
   if ((st = h->part_i.ensure(static_cast<size_t>(plan.partial_bytes / 2))) != KNN_OK) return st;
   if (cq == 0 && (st = h->q32.ensure(static_cast<size_t>(nq) * h->dim * 4)) != KNN_OK) return st;
@@ -1174,7 +1178,7 @@ int knn_index_destroy(knn_index* h) {
   if (h->comm) nccl().CommDestroy(h->comm);
   for (DevBuf* b : {&h->q32, &h->q16, &h->qnorm, &h->part_d, &h->part_i, &h->out_d, &h->out_i,
                     &h->gather_send, &h->gather_recv, &h->cand_d, &h->cand_i, &h->rr_d,
-                    &h->rr_i, &h->pilot, &h->thr, &h->xdec})
+                    &h->rr_i, &h->pilot, &h->thr, &h->xdec, &h->bound})
     b->release();
   if (h->data) cudaFree(h->data);
   if (h->norms) cudaFree(h->norms);
@@ -1583,6 +1587,7 @@ int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
   p.pilot = 0;
   p.pilot_out = nullptr;
   p.thr_init = nullptr;
+  p.bound = nullptr;
   KNN_CUDA(knn::launch_scan(qmap, h->xmap, p, plan, h->stream));
   KNN_CUDA(knn::launch_merge(part_d, part_i, k, plan.splits * k, static_cast<int>(plan.splits),
                              static_cast<int>(k), nq, h->row_offset, out_d, out_i, false,

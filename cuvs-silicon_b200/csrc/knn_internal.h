@@ -51,6 +51,10 @@ struct ScanParams {
   float* pilot_out;
   // Main pass: per-query starting threshold (nullptr: none).
   const float* thr_init;
+  // Per-query bound shared by all CTAs (nullptr: none), as order-preserving
+  // bits of a distance B such that some unit holds k rows at d <= B;
+  // 0xFFFFFFFF = none yet.  Reset by the query conversion of each search.
+  uint32_t* bound;
 };
 
 // k above which a search runs the pilot pass first (see knn_scan.cu).
@@ -81,10 +85,13 @@ cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
 
 // fp32/fp16 rows -> fp16 rows with leading dimension ld (zero padded) plus
 // fp32 norms of the rounded rows.  in_is_half selects the input type.
-// Output rows [rows, rows_out) are written as zeros (no norm).
+// Output rows [rows, rows_out) are written as zeros (no norm).  fill
+// (optional): fill_n words set to 0xFFFFFFFF (the scan's shared per-query
+// bounds, reset by the query conversion of every search).
 cudaError_t launch_convert_rows(const void* in, bool in_is_half, int64_t rows,
                                 int64_t rows_out, int64_t dim, __half* out, int64_t ld,
-                                float* norms, cudaStream_t stream);
+                                float* norms, cudaStream_t stream, uint32_t* fill = nullptr,
+                                int64_t fill_n = 0);
 
 // Rows of the fp16 query buffer a search needs: every 128-row query slab
 // the scan kernel loads lies inside it, so no TMA box leaves the buffer.

@@ -37,13 +37,18 @@ __device__ __forceinline__ float load_elem(const void* in, int64_t i) {
 template <bool kHalfIn>
 __global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, int64_t rows_out,
                                     int64_t dim, __half* __restrict__ out, int64_t ld,
-                                    float* __restrict__ norms, bool vec) {
+                                    float* __restrict__ norms, bool vec,
+                                    uint32_t* __restrict__ fill, int64_t fill_n) {
   // Let the next kernel (the scan) be scheduled now: its dataset loads do
   // not depend on this kernel, and it waits before reading the queries.
   // This kernel is itself a programmatic dependent of the previous search's
   // kernels, which may still read `out`: wait for them before writing.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // per-search state of the scan that follows (its shared per-query bounds)
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < fill_n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    fill[i] = 0xFFFFFFFFu;
   const int lane = threadIdx.x & 31;
   const int64_t warps_per_block = blockDim.x >> 5;
   const int64_t first = static_cast<int64_t>(blockIdx.x) * warps_per_block + (threadIdx.x >> 5);
@@ -111,7 +116,7 @@ __global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, i
 
 cudaError_t launch_convert_rows(const void* in, bool in_is_half, int64_t rows, int64_t rows_out,
                                 int64_t dim, __half* out, int64_t ld, float* norms,
-                                cudaStream_t stream) {
+                                cudaStream_t stream, uint32_t* fill, int64_t fill_n) {
   if (rows_out < rows) rows_out = rows;
   if (rows_out <= 0) return cudaSuccess;
   const bool vec = (dim % 8 == 0) && ((reinterpret_cast<uintptr_t>(in) & 15u) == 0) &&
@@ -131,9 +136,9 @@ cudaError_t launch_convert_rows(const void* in, bool in_is_half, int64_t rows, i
   cfg.numAttrs = 1;
   if (in_is_half)
     return cudaLaunchKernelEx(&cfg, convert_rows_kernel<true>, in, rows, rows_out, dim, out, ld,
-                              norms, vec);
+                              norms, vec, fill, fill ? fill_n : int64_t(0));
   return cudaLaunchKernelEx(&cfg, convert_rows_kernel<false>, in, rows, rows_out, dim, out, ld,
-                            norms, vec);
+                            norms, vec, fill, fill ? fill_n : int64_t(0));
 }
 
 }  // namespace knn

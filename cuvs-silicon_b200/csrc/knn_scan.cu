@@ -288,6 +288,16 @@ __device__ __forceinline__ float dist_from_dot(uint32_t acc_bits, float qn, floa
   }
 }
 
+// Order-preserving 32-bit image of a distance (any sign) and its inverse;
+// used for the per-query bound the CTAs share through atomicMin.
+__device__ __forceinline__ uint32_t dist_order_bits(float d) {
+  const uint32_t u = __float_as_uint(d);
+  return u ^ ((u >> 31) ? 0xFFFFFFFFu : 0x80000000u);
+}
+__device__ __forceinline__ float dist_from_order_bits(uint32_t b) {
+  return __uint_as_float(b ^ ((b >> 31) ? 0x80000000u : 0xFFFFFFFFu));
+}
+
 // Smallest float above a finite t (t is never -0 here).
 __device__ __forceinline__ float next_up(float t) {
   const int b = __float_as_int(t);
@@ -327,6 +337,7 @@ struct RowState {
   uint64_t root; // heap root key (worst kept entry) once the heap holds k, else empty
   int cnt;       // survivors waiting in the row's buffer
   int size;      // entries in the heap (<= k)
+  uint32_t pub;  // bound this row last published (order bits)
 };
 
 // Moves every lane's buffered survivors into its heap.  Warp-uniform: all
@@ -370,6 +381,13 @@ __device__ __forceinline__ void flush_buffer(RowState& st, const Smem& sm, int k
 // writes its 32 sorted group minima to p.pilot_out for
 // pilot_threshold_kernel.  A main pass started with p.thr_init filters
 // every tile from the first one with that per-query threshold.
+// Shared bound (p.bound): once a row's heap holds k entries, its k-th
+// distance R bounds the query's k-th distance over the whole shard (this
+// unit alone has k rows at d <= R), so the CTA publishes R with atomicMin
+// and every CTA filters with the smallest published R from its next tile
+// on.  A row of the final top-k lies at d <= R and still passes in its own
+// unit, whose best k then include it; units may end with fewer than k
+// entries (padding), which the merge ignores.
 template <int kMetric>
 __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base, int warp,
                          int lane) {
@@ -393,6 +411,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
     st.root = empty_key<kMetric>();
     st.cnt = 0;
     st.size = 0;
+    st.pub = 0xFFFFFFFFu;
     // Row norms are prefetched one tile ahead into registers, then staged in
     // this warp's slice of shared memory so the chunk loop reads them with
     // a shared-memory load instead of waiting on DRAM once per chunk (for
@@ -421,6 +440,8 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
         break;
       }
       tc_fence_after();
+      uint32_t shared_b = 0xFFFFFFFFu;  // read now, applied before the chunk loop
+      if (p.bound && valid_q) shared_b = *reinterpret_cast<volatile const uint32_t*>(p.bound + q);
       if (warp_active) {
 #pragma unroll
         for (int c = 0; c < kAccCols / 32; ++c) ns[c * 32 + lane] = nx[c];
@@ -503,6 +524,10 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
         // TMEM loads double-buffered: chunk c + 1 is in flight while chunk c
         // is processed.
         static_assert((kAccCols / 32) % 2 == 0, "chunk pairs");
+        if (shared_b != 0xFFFFFFFFu) {
+          const float bnd = dist_from_order_bits(shared_b);
+          if (bnd < kInf) st.thr = fminf(st.thr, next_up(bnd));
+        }
         if (!p.pilot) {  // uniform over the grid: the warp stays converged
           uint32_t ra[32], rb[32];
           tmem_ld_32x32b_x32(tbase, ra);
@@ -524,7 +549,16 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
       ++tc;
       // survivors enter the heap at every tile end so thr tightens early (the
       // accumulator is already released; this overlaps the next tile's MMAs)
-      if (warp_active && __any_sync(0xffffffffu, st.cnt > 0)) flush_buffer<kMetric>(st, sm, k, stride, row);
+      if (warp_active && __any_sync(0xffffffffu, st.cnt > 0)) {
+        flush_buffer<kMetric>(st, sm, k, stride, row);
+        if (p.bound && valid_q && st.size == k) {
+          const uint32_t bits = dist_order_bits(key_dist<kMetric>(st.root));
+          if (bits < st.pub) {
+            atomicMin(p.bound + q, bits);
+            st.pub = bits;
+          }
+        }
+      }
     }
     if (failed) break;
     if (p.pilot) continue;
