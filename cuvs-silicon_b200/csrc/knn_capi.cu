@@ -137,6 +137,18 @@ int64_t row_ld(int64_t dim) {
   return (dim + 7) / 8 * 8;
 }
 
+// Device address of page-locked host memory (nullptr for anything else).
+// Page-locked memory is addressable by the device under unified virtual
+// addressing, so kernels may read or write it in place.
+void* pinned_device_ptr(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
+}
+
 // 0 = host memory, 1 = device memory of `device`, -1 = other device.
 int classify(const void* p, int device) {
   cudaPointerAttributes a;
@@ -250,6 +262,7 @@ struct knn_index {
     const void* queries;
     const void* neighbors;
     const void* distances;
+    int in_place;  // bit 0: queries, bit 1: outputs used in place (page-locked host memory)
     int64_t nq, k, ks;
     bool i64;
     cudaStream_t stream;
@@ -482,6 +495,10 @@ int check_device_error(knn_index* h) {
     *h->err_host = 0;
     cudaMemsetAsync(h->err_dev, 0, sizeof(int), h->stream);
     cudaStreamSynchronize(h->stream);
+    if (code == knn::kErrTimeoutPeer)
+      return fail(KNN_ETIMEOUT,
+                  "a peer's list did not arrive within the 1 s bound (device code %d); "
+                  "attach the communicator again before the next search", code);
     return fail(KNN_ETIMEOUT, "scan kernel gave up on a bounded wait (device code %d)", code);
   }
   return KNN_OK;
@@ -667,6 +684,18 @@ int search_pass(knn_index* h, const float* queries, int64_t nq, int64_t k, int64
   const int pst = knn::plan_search(h->n, h->dim, nq, ks, h->num_sms, &plan);
   if (pst != 0) return fail(pst, "k = %lld is outside the engine's limits", (long long)ks);
 
+  // Page-locked host buffers are used in place: the query conversion reads
+  // the queries from host memory and the last kernel writes the results
+  // there, with no staging copies (the re-rank kernel, which reads the fp32
+  // queries many times, keeps the device copy).
+  const void* q_pin = cq == 0 && !rerank ? pinned_device_ptr(queries) : nullptr;
+  void* d_pin = cd == 0 && cn == 0 ? pinned_device_ptr(distances) : nullptr;
+  void* n_pin = d_pin ? pinned_device_ptr(neighbors) : nullptr;
+  if (!n_pin) d_pin = nullptr;
+  // which host buffers are used in place (a graph key: a buffer that is no
+  // longer page-locked must not be replayed into)
+  const int in_place = (q_pin ? 1 : 0) | (d_pin ? 2 : 0);
+
   // scratch: everything is sized before any work is enqueued or captured
   const size_t qk = static_cast<size_t>(nq) * k;
   const size_t idx_bytes = qk * (out_i64 ? 8 : 4);
@@ -681,9 +710,10 @@ int search_pass(knn_index* h, const float* queries, int64_t nq, int64_t k, int64
   if ((st = h->bound.ensure(static_cast<size_t>(nq) * 4)) != KNN_OK) return st;
   if ((st = h->part_d.ensure(static_cast<size_t>(plan.partial_bytes / 2))) != KNN_OK) return st;
   if ((st = h->part_i.ensure(static_cast<size_t>(plan.partial_bytes / 2))) != KNN_OK) return st;
-  if (cq == 0 && (st = h->q32.ensure(static_cast<size_t>(nq) * h->dim * 4)) != KNN_OK) return st;
-  if (cd == 0 && (st = h->out_d.ensure(qk * 4)) != KNN_OK) return st;
-  if (cn == 0 && (st = h->out_i.ensure(idx_bytes)) != KNN_OK) return st;
+  if (cq == 0 && !q_pin && (st = h->q32.ensure(static_cast<size_t>(nq) * h->dim * 4)) != KNN_OK)
+    return st;
+  if (cd == 0 && !d_pin && (st = h->out_d.ensure(qk * 4)) != KNN_OK) return st;
+  if (cn == 0 && !n_pin && (st = h->out_i.ensure(idx_bytes)) != KNN_OK) return st;
   if (h->comm) {
     if ((st = h->gather_send.ensure(qk * 8)) != KNN_OK) return st;
     if ((st = h->gather_recv.ensure(qk * 8 * h->n_ranks)) != KNN_OK) return st;
@@ -710,30 +740,34 @@ int search_pass(knn_index* h, const float* queries, int64_t nq, int64_t k, int64
   }
 
   const float* qsrc = queries;
-  if (cq == 0) {
+  if (q_pin) {
+    qsrc = static_cast<const float*>(q_pin);
+  } else if (cq == 0) {
     KNN_CUDA(cudaMemcpyAsync(h->q32.ptr, queries, static_cast<size_t>(nq) * h->dim * 4,
                              cudaMemcpyHostToDevice, h->stream));
     qsrc = h->q32.as<float>();
   }
-  float* dst_d = cd == 0 ? h->out_d.as<float>() : distances;
-  void* dst_i = cn == 0 ? h->out_i.ptr : neighbors;
+  float* dst_d = d_pin ? static_cast<float*>(d_pin) : cd == 0 ? h->out_d.as<float>() : distances;
+  void* dst_i = n_pin ? n_pin : cn == 0 ? h->out_i.ptr : neighbors;
 
   int launches = 0;
   std::array<cudaEvent_t, 3>* prof = nullptr;
   if (h->profiling) {
     if ((st = next_profile_slot(h, &prof)) != KNN_OK) return st;
   }
-  // Replay a graph for device-resident searches that repeat buffers + shape.
-  // Not with a communicator: replaying the captured all-gather measured
-  // slower than launching it directly (8 ranks on one NVSwitch node).
-  const bool graphable =
-      h->use_graphs && !prof && !h->comm && cq == 1 && cn == 1 && cd == 1;
+  // Replay a graph for searches that repeat buffers + shape.  Host buffers
+  // qualify too: the graph reads and writes either them in place (page-
+  // locked, part of the key) or the staging buffers (whose reallocation
+  // bumps the generation).  Not with a communicator: replaying the captured
+  // all-gather measured slower than launching it directly (8 ranks on one
+  // NVSwitch node).
+  const bool graphable = h->use_graphs && !prof && !h->comm;
   knn_index::GraphEntry* hit = nullptr;
   if (graphable) {
     for (auto& g : h->graphs) {
       if (g.queries == queries && g.neighbors == neighbors && g.distances == distances &&
-          g.nq == nq && g.k == k && g.ks == ks && g.i64 == out_i64 && g.stream == h->stream &&
-          g.generation == h->generation) {
+          g.in_place == in_place && g.nq == nq && g.k == k && g.ks == ks && g.i64 == out_i64 &&
+          g.stream == h->stream && g.generation == h->generation) {
         hit = &g;
         break;
       }
@@ -748,8 +782,8 @@ int search_pass(knn_index* h, const float* queries, int64_t nq, int64_t k, int64
         if (h->graphs.front().exec) cudaGraphExecDestroy(h->graphs.front().exec);
         h->graphs.erase(h->graphs.begin());
       }
-      h->graphs.push_back({queries, neighbors, distances, nq, k, ks, out_i64, h->stream,
-                           h->generation, 0, nullptr});
+      h->graphs.push_back({queries, neighbors, distances, in_place, nq, k, ks, out_i64,
+                           h->stream, h->generation, 0, nullptr});
       goto direct;
     }
     if (!hit) {
@@ -771,8 +805,8 @@ int search_pass(knn_index* h, const float* queries, int64_t nq, int64_t k, int64
           if (h->graphs.front().exec) cudaGraphExecDestroy(h->graphs.front().exec);
           h->graphs.erase(h->graphs.begin());
         }
-        h->graphs.push_back({queries, neighbors, distances, nq, k, ks, out_i64, h->stream,
-                             h->generation, launches, exec});
+        h->graphs.push_back({queries, neighbors, distances, in_place, nq, k, ks, out_i64,
+                             h->stream, h->generation, launches, exec});
         hit = &h->graphs.back();
       } else {
         // capture is not available here: run searches directly from now on
@@ -795,9 +829,9 @@ direct:
     KNN_CUDA(cudaMemcpyAsync(h->uncert_host, h->uncert_dev, sizeof(int), cudaMemcpyDeviceToHost,
                              h->stream));
 
-  if (cd == 0)
+  if (cd == 0 && !d_pin)
     KNN_CUDA(cudaMemcpyAsync(distances, dst_d, qk * 4, cudaMemcpyDeviceToHost, h->stream));
-  if (cn == 0)
+  if (cn == 0 && !n_pin)
     KNN_CUDA(cudaMemcpyAsync(neighbors, dst_i, idx_bytes, cudaMemcpyDeviceToHost, h->stream));
   g_dispatch.fetch_add(launches);
   h->kernel_launches += launches;

@@ -203,6 +203,37 @@ def test_graph_replay_follows_buffer_contents(engine, oracle_mod, torch_cuda):
         assert np.array_equal(i, ref[name][0]) and np.array_equal(d, ref[name][1])
 
 
+def test_pinned_host_buffers_in_place(engine, oracle_mod, torch_cuda):
+    """Page-locked host queries and outputs are used in place by the kernels
+    (no staging copies) and replayed from a CUDA graph; results equal the
+    pageable-buffer path byte for byte and follow the buffers' contents."""
+    torch = torch_cuda
+    rng = np.random.Generator(np.random.PCG64(31))
+    base = rng.standard_normal((9000, 200), dtype=np.float32)
+    qa = rng.standard_normal((30, 200), dtype=np.float32)
+    qb = rng.standard_normal((30, 200), dtype=np.float32)
+    with engine.Index(0) as idx:
+        idx.build(base)
+        ref = {name: idx.search(q, 12) for name, q in (("a", qa), ("b", qb))}
+        qp = torch.empty((30, 200), dtype=torch.float32).pin_memory()
+        ip = torch.empty((30, 12), dtype=torch.int32).pin_memory()
+        dp = torch.empty((30, 12), dtype=torch.float32).pin_memory()
+        for name, src in (("a", qa), ("a", qa), ("b", qb), ("a", qa), ("b", qb)):
+            qp.copy_(torch.from_numpy(src))
+            idx.search(qp, 12, neighbors=ip, distances=dp)
+            assert np.array_equal(ip.numpy().view(np.uint32), ref[name][0]), name
+            assert np.array_equal(dp.numpy(), ref[name][1]), name
+        # pinned queries with pageable outputs, and the reverse
+        qp.copy_(torch.from_numpy(qb))
+        i, d = idx.search(qp, 12)
+        assert np.array_equal(i, ref["b"][0]) and np.array_equal(d, ref["b"][1])
+        idx.search(qa, 12, neighbors=ip, distances=dp)
+        assert np.array_equal(ip.numpy().view(np.uint32), ref["a"][0])
+    b16, q16, oi, od = _check(oracle_mod, base, qa, 12)
+    par = oracle_mod.check_parity(b16, q16, ref["a"][0], ref["a"][1], oi, od, REL_TOL)
+    assert par.ok, par.detail
+
+
 def test_repeat_is_bit_identical(engine, oracle_mod, torch_cuda):
     """Deterministic: two searches give the same bytes (run-twice check)."""
     rng = np.random.Generator(np.random.PCG64(9))
