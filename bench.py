@@ -248,7 +248,8 @@ def run_reference(a):
         "data": "synthetic: unit-norm Gaussian mixture (numpy PCG64, seeds 11/12/13), "
                 "fp16-rounded, fp32 on host",
         "config": {"workload": workload_name(a), "n_rows": a.n, "dim": a.dim,
-                   "n_queries": a.q, "k": a.k,
+                   "n_queries": a.q, "k": a.k, "metric": "L2Expanded",
+                   "exact_fp32_rerank": False,
                    "sample": f"{sample} queries per step x all {a.n} rows"},
         "cpu_baseline": {"value": qps, "unit": UNIT, "cores": min(threads, sample),
                          "kind": kind,
