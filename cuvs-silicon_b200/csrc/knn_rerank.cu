@@ -90,6 +90,105 @@ __device__ float exact_dist(const float* __restrict__ q, const float* __restrict
   }
 }
 
+// Cooperative path (dim % 4 == 0, 16-byte aligned rows and queries): the
+// block copies the candidate rows into shared memory chunk by chunk with
+// cp.async (kRerankStages chunks in flight, coalesced 16-byte copies; rows
+// padded by one float4 so 8 consecutive lanes read distinct banks), and
+// thread t sums candidate t's chunk from there.  Every thread still adds
+// the dimensions of its row in index order, so the values equal
+// exact_dist's.
+constexpr int kRerankStages = 4;
+constexpr int kRerankStageBytes = 40960;
+
+// float4 per row per chunk for kc candidates (at most 64, at least 1).
+inline int rerank_chunk_f4(int kc, int64_t dim) {
+  int cw = kRerankStageBytes / (16 * kc) - 1;
+  if (cw > 64) cw = 64;
+  if (cw > dim / 4) cw = static_cast<int>(dim / 4);
+  return cw < 1 ? 1 : cw;
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t sa = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Called by every thread of the block; returns candidate t's distance for
+// t < kc with a valid row (s_i[t] != kNoIndex), +inf otherwise.
+template <int kMetric>
+__device__ float staged_dist(const float* __restrict__ qv, const float* __restrict__ rows,
+                             int64_t dim, const uint32_t* s_i, int kc, int cw, float4* buf) {
+  const int t = threadIdx.x;
+  const int64_t d4 = dim / 4;
+  const int nch = static_cast<int>((d4 + cw - 1) / cw);
+  const int rs = cw + 1;
+  const int stage_f4 = kc * rs;
+  auto issue = [&](int c) {
+    if (c < nch) {
+      float4* dst = buf + (c % kRerankStages) * stage_f4;
+      const int64_t w0 = static_cast<int64_t>(c) * cw;
+      const int wn = static_cast<int>(d4 - w0 < cw ? d4 - w0 : cw);
+      for (int e = t; e < kc * wn; e += blockDim.x) {
+        const int r = e / wn;
+        const int w = e - r * wn;
+        const uint32_t row = s_i[r];
+        if (row != kNoIndex)
+          cp_async16(dst + r * rs + w, rows + static_cast<int64_t>(row) * dim + (w0 + w) * 4);
+      }
+    }
+    cp_async_commit();  // one group per call, empty or not: uniform counting
+  };
+  for (int c = 0; c < kRerankStages - 1; ++c) issue(c);
+  const bool mine = t < kc && s_i[t] != kNoIndex;
+  const float4* q4 = reinterpret_cast<const float4*>(qv);
+  float acc = 0.0f;
+  for (int c = 0; c < nch; ++c) {
+    cp_async_wait<kRerankStages - 2>();  // this thread's copies of chunk c
+    __syncthreads();                     // everyone's
+    if (mine) {
+      const float4* src = buf + (c % kRerankStages) * stage_f4 + t * rs;
+      const int64_t w0 = static_cast<int64_t>(c) * cw;
+      const int wn = static_cast<int>(d4 - w0 < cw ? d4 - w0 : cw);
+      for (int w = 0; w < wn; ++w) {
+        const float4 a = __ldg(q4 + w0 + w);
+        const float4 b = src[w];
+        if constexpr (kMetric == KNN_METRIC_INNER_PRODUCT) {
+          acc = __fadd_rn(acc, __fmul_rn(a.x, b.x));
+          acc = __fadd_rn(acc, __fmul_rn(a.y, b.y));
+          acc = __fadd_rn(acc, __fmul_rn(a.z, b.z));
+          acc = __fadd_rn(acc, __fmul_rn(a.w, b.w));
+        } else {
+          float u;
+          u = __fsub_rn(a.x, b.x);
+          acc = __fadd_rn(acc, __fmul_rn(u, u));
+          u = __fsub_rn(a.y, b.y);
+          acc = __fadd_rn(acc, __fmul_rn(u, u));
+          u = __fsub_rn(a.z, b.z);
+          acc = __fadd_rn(acc, __fmul_rn(u, u));
+          u = __fsub_rn(a.w, b.w);
+          acc = __fadd_rn(acc, __fmul_rn(u, u));
+        }
+      }
+    }
+    __syncthreads();                     // chunk c's stage may be refilled
+    issue(c + kRerankStages - 1);
+  }
+  cp_async_wait<0>();
+  if (!mine) return __int_as_float(0x7f800000);
+  if constexpr (kMetric == KNN_METRIC_INNER_PRODUCT) {
+    return acc == 0.0f ? 0.0f : -acc;
+  } else {
+    return acc;
+  }
+}
+
 // Bound of |d16(y) - d32(y)| for squared L2 over rows y with d32(y) <= r.
 // qn = |q| of the fp32 query, xn >= |x| of every fp32 row, D = dim,
 // u = 2^-24 (fp32 unit roundoff):
@@ -131,7 +230,7 @@ __global__ void __launch_bounds__(kRerankThreads)
                   const uint32_t* __restrict__ cand_i, int kc, int k,
                   const float* __restrict__ max_norm2, int64_t index_offset,
                   float* __restrict__ out_d, OutIdx* __restrict__ out_i, float sign,
-                  int* __restrict__ uncertified) {
+                  int* __restrict__ uncertified, int cw) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ float s_d[kRerankThreads];
@@ -157,18 +256,19 @@ __global__ void __launch_bounds__(kRerankThreads)
   for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
   if ((t & 31) == 0) s_red[t >> 5] = part;
 
-  float d = __int_as_float(0x7f800000);
   uint32_t idx = kNoIndex;
-  if (t < kc) {
-    const uint32_t c = cand_i[q * kc + t];
-    if (c != kNoIndex) {
-      idx = c;
-      d = exact_dist<kMetric>(qv, rows + static_cast<int64_t>(c) * dim, dim, vec4);
-      atomicAdd(&s_valid, 1);
-    }
+  if (t < kc) idx = cand_i[q * kc + t];
+  s_i[t] = idx;
+  if (idx != kNoIndex) atomicAdd(&s_valid, 1);
+  __syncthreads();
+  float d = __int_as_float(0x7f800000);
+  if (cw > 0) {  // uniform: the launcher picks the path
+    extern __shared__ float4 rr_buf[];
+    d = staged_dist<kMetric>(qv, rows, dim, s_i, kc, cw, rr_buf);
+  } else if (idx != kNoIndex) {
+    d = exact_dist<kMetric>(qv, rows + static_cast<int64_t>(idx) * dim, dim, vec4);
   }
   s_d[t] = d;
-  s_i[t] = idx;
   __syncthreads();
   const int valid = s_valid;
 
@@ -224,9 +324,27 @@ cudaError_t launch_t(const float* queries, const float* rows, int64_t dim,
                      int64_t n_queries, const float* max_norm2, int64_t index_offset,
                      float* out_d, OutIdx* out_i, float sign, int* uncertified,
                      cudaStream_t stream) {
+  // cooperative staging when rows and queries allow 16-byte copies
+  const bool vec4 = (dim % 4) == 0 && (reinterpret_cast<uintptr_t>(queries) % 16) == 0 &&
+                    (reinterpret_cast<uintptr_t>(rows) % 16) == 0;
+  const int cw = vec4 ? rerank_chunk_f4(kc, dim) : 0;
+  const size_t smem =
+      vec4 ? static_cast<size_t>(kRerankStages) * kc * (cw + 1) * 16 : size_t(0);
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    e = cudaFuncSetAttribute(rerank_kernel<kMetric, OutIdx>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kRerankStages * kRerankStageBytes);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(n_queries));
   cfg.blockDim = dim3(kRerankThreads);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -235,7 +353,7 @@ cudaError_t launch_t(const float* queries, const float* rows, int64_t dim,
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, rerank_kernel<kMetric, OutIdx>, queries, rows, dim, cand_d,
                             cand_i, kc, k, max_norm2, index_offset, out_d, out_i, sign,
-                            uncertified);
+                            uncertified, cw);
 }
 
 // Largest |x16|^2 over the rows (norms are >= 0 or NaN/inf, so their bit
