@@ -1351,6 +1351,11 @@ int knn_index_rerank_stats(knn_index* h, int64_t* uncertified, int64_t* widened)
   return KNN_OK;
 }
 
+double knn_rerank_bound(int metric, double r, double query_norm, double row_norm, int64_t dim) {
+  if (dim <= 0 || query_norm < 0 || row_norm < 0) return -1.0;
+  return knn::rerank_bound(metric, r, query_norm, row_norm, dim);
+}
+
 int knn_plan_search(int64_t n_rows, int64_t dim, int64_t nq, int64_t k, int num_sms,
                     knn_plan* out) {
   if (!out) return fail(KNN_EINVAL, "null plan");

@@ -163,6 +163,10 @@ cudaError_t launch_rerank(const float* queries, const float* rows, int64_t dim,
                           int64_t index_offset, float* out_d, void* out_i, bool out_i64,
                           bool negate_out, int* uncertified, cudaStream_t stream);
 
+// The certificate's bound of |scan distance - fp32 distance| (knn_rerank.cu)
+// for a row that could beat a re-ranked distance r; qn = |q|, xn >= |x|.
+double rerank_bound(int metric, double r, double qn, double xn, int64_t dim);
+
 // out = the largest of norms[0..n) (norms >= 0).
 cudaError_t launch_max_norm(const float* norms, int64_t n, float* out, cudaStream_t stream);
 

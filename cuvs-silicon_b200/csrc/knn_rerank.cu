@@ -201,7 +201,7 @@ __device__ float staged_dist(const float* __restrict__ qv, const float* __restri
 //        two units in the last place), the final fma and add 2u (qn + xn)^2;
 //   the reference's own sum: |d32 - d| <= (D + 3) u d, so d <= r / (1 - g).
 // A 1.25 factor covers the rounding of this bound itself.
-__device__ double bound_l2(double r, double qn, double xn, int64_t dim) {
+__host__ __device__ double bound_l2(double r, double qn, double xn, int64_t dim) {
   const double u = 5.9604644775390625e-08;  // 2^-24
   const double D = static_cast<double>(dim);
   const double g = (D + 3.0) * u;
@@ -215,7 +215,7 @@ __device__ double bound_l2(double r, double qn, double xn, int64_t dim) {
 // Same for the inner product (d = -score):
 //   |q16.x16 - q.x| <= |q16 - q| |x16| + |q| |x16 - x| <= 2^-10 qn xn + subnormal terms;
 //   tensor-core dot 4 D u qn xn; the reference's sum (D + 1) u qn xn.
-__device__ double bound_ip(double qn, double xn, int64_t dim) {
+__host__ __device__ double bound_ip(double qn, double xn, int64_t dim) {
   const double u = 5.9604644775390625e-08;
   const double D = static_cast<double>(dim);
   const double sub = sqrt(D) * 2.98023223876953125e-08;
@@ -394,6 +394,10 @@ cudaError_t launch_rerank(const float* queries, const float* rows, int64_t dim,
   return launch_t<KNN_METRIC_L2_EXPANDED, uint32_t>(
       queries, rows, dim, cand_d, cand_i, kc, k, n_queries, max_norm2, index_offset, out_d,
       static_cast<uint32_t*>(out_i), sign, uncertified, stream);
+}
+
+double rerank_bound(int metric, double r, double qn, double xn, int64_t dim) {
+  return metric == KNN_METRIC_INNER_PRODUCT ? bound_ip(qn, xn, dim) : bound_l2(r, qn, xn, dim);
 }
 
 cudaError_t launch_max_norm(const float* norms, int64_t n, float* out, cudaStream_t stream) {

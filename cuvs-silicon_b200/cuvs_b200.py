@@ -92,6 +92,8 @@ def lib() -> ctypes.CDLL:
         "knn_index_reset_kernel_stats": (I, [P]),
         "knn_index_set_rerank": (I, [P, I]),
         "knn_index_build_file": (I, [P, ctypes.c_char_p, I, I, I, I]),
+        "knn_rerank_bound": (ctypes.c_double, [I, ctypes.c_double, ctypes.c_double,
+                                               ctypes.c_double, I64]),
         "knn_index_rerank_stats": (I, [P, ctypes.POINTER(I64), ctypes.POINTER(I64)]),
         "knn_index_search_noalloc": (I, [P, P, I64, I64, P, P]),
         "knn_selftest_bounded_wait": (I, [I, I64]),
@@ -353,3 +355,8 @@ def read_bin(path: str, dtype=np.float32) -> np.ndarray:
     if rows < 0 or cols < 0 or raw.size != 2 + rows * cols:
         raise ValueError(f"{path}: shape {rows} x {cols} does not match the file")
     return raw[2:].view(dtype).reshape(rows, cols).copy()
+
+
+def rerank_bound(metric: int, r: float, query_norm: float, row_norm: float, dim: int) -> float:
+    """The exact re-rank certificate's bound (knn_rerank_bound)."""
+    return float(lib().knn_rerank_bound(metric, r, query_norm, row_norm, dim))

@@ -227,6 +227,14 @@ int knn_index_set_rerank(knn_index* index, int enabled);
  * with the first candidate count (and so were searched again). */
 int knn_index_rerank_stats(knn_index* index, int64_t* uncertified, int64_t* widened);
 
+/* The re-rank certificate's bound on |scan distance - fp32 distance| for a
+ * row whose fp32 distance does not exceed r (for the inner product, on the
+ * scores), given |q| = query_norm and |x| <= row_norm; the same function
+ * the kernel evaluates.  Pure host arithmetic, exposed for tests; -1 on
+ * invalid arguments.  No counterpart in the reference. */
+double knn_rerank_bound(int metric, double r, double query_norm, double row_norm,
+                        int64_t dim);
+
 /* Plans a search without running it (pure host arithmetic).  num_sms <= 0
  * uses 148 (B200).  No counterpart in the reference. */
 int knn_plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k,
