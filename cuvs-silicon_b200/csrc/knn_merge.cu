@@ -28,6 +28,7 @@
 // in the stream and waits (griddepcontrol.wait) before reading its input.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "knn_internal.h"
@@ -522,7 +523,7 @@ cudaError_t launch_e(const float* in_d, const uint32_t* in_i, int64_t stride_lis
   static_assert(kCandCap <= kStageEntries, "candidates fit the staging area");
   constexpr size_t smem = static_cast<size_t>(kStageEntries) * 8;
   // opt in to more than 48 KiB of dynamic shared memory once per device
-  static bool configured[64][2] = {};
+  static std::atomic<bool> configured[64][2] = {};  // set once; idempotent
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;

@@ -28,6 +28,7 @@
 // sequential), ordered by (-score, index); the reported value is the score.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "knn_internal.h"
@@ -330,7 +331,7 @@ cudaError_t launch_t(const float* queries, const float* rows, int64_t dim,
   const int cw = vec4 ? rerank_chunk_f4(kc, dim) : 0;
   const size_t smem =
       vec4 ? static_cast<size_t>(kRerankStages) * kc * (cw + 1) * 16 : size_t(0);
-  static bool configured[64] = {};
+  static std::atomic<bool> configured[64] = {};  // set once; idempotent
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;

@@ -34,6 +34,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "knn_internal.h"
@@ -775,7 +776,7 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
 cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap, const ScanParams& p,
                         const Plan& plan, cudaStream_t stream, bool overlap) {
   // the opt-in shared-memory limit is a per-device function attribute
-  static bool configured[64] = {};
+  static std::atomic<bool> configured[64] = {};  // set once; idempotent
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
