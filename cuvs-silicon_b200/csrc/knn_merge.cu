@@ -41,6 +41,7 @@ constexpr int kMergeWarps = 8;
 constexpr int kStageEntries = 6144;  // 48 KiB of (fp32, uint32) entries (fold path)
 constexpr int kSelCap = 2048;        // lists' j-th entries (threshold path)
 constexpr int kCandCap = 4096;       // threshold-path candidates
+constexpr int kRankPlaceMax = 1024;  // candidates ordered by rank counting (4 per thread)
 static_assert(kSelCap + kCandCap <= kStageEntries, "threshold arrays share the stage");
 
 __device__ __forceinline__ bool less_pair(float da, uint32_t ia, float db, uint32_t ib) {
@@ -185,8 +186,8 @@ __device__ __forceinline__ void block_sort(float* d, uint32_t* i, int p2) {
 // stored.  Called by every thread; ends with a block barrier.
 __device__ __forceinline__ void rank_place(const float* in_d, const uint32_t* in_i, int n,
                                            float* out_d, uint32_t* out_i, int limit) {
-  const int t = threadIdx.x;
-  if (t < n) {
+  // n <= kRankPlaceMax: thread t ranks entries t, t + blockDim.x, ...
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
     const float d = in_d[t];
     const uint32_t i = in_i[t];
     int rank = 0;
@@ -425,6 +426,37 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
   // tau is the padding, i.e. when fewer than r lists have j entries)
   const int total = n_lists * k;
   constexpr int kPer = 8;  // entries per thread per round, loaded before use
+  if (n_lists <= static_cast<int>(blockDim.x)) {
+    // The lists are sorted, so a list's candidates are a prefix of it:
+    // thread l reads list l four entries at a time (independent loads) and
+    // stops at the first entry above tau or at the padding.
+    if (tid < n_lists) {
+      const float* lsd = qd + static_cast<int64_t>(tid) * stride_list;
+      const uint32_t* lsi = qi + static_cast<int64_t>(tid) * stride_list;
+      bool more = true;
+      for (int e0 = 0; e0 < k && more; e0 += 4) {
+        float dv[4];
+        uint32_t iv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int e = e0 + u;
+          dv[u] = e < k ? lsd[e] : kInf;
+          iv[u] = e < k ? lsi[e] : kNoIndex;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          more = more && iv[u] != kNoIndex && (dv[u] < td || (dv[u] == td && iv[u] <= ti));
+          if (more) {
+            const int pos = atomicAdd(&s_count, 1);
+            if (pos < kCandCap) {
+              cd[pos] = dv[u];
+              ci[pos] = iv[u];
+            }
+          }
+        }
+      }
+    }
+  } else {
   for (int e0 = 0; e0 < total; e0 += kPer * kMergeWarps * 32) {
     float dv[kPer];
     uint32_t iv[kPer];
@@ -460,6 +492,7 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
       }
     }
   }
+  }
   __syncthreads();
   const int count = s_count;
   if (count > kCandCap) {  // block-uniform
@@ -469,7 +502,7 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
     emit_result(ex, q, k, cd, ci, k, index_offset, out_d, out_i, sign);
     return;
   }
-  if (count <= static_cast<int>(blockDim.x)) {
+  if (count <= kRankPlaceMax) {
     // candidates are distinct (distinct row indices): rank counting places
     // the first k of them, sorted, in front of the selection array
     rank_place(cd, ci, count, seld, seli, k);
