@@ -49,3 +49,14 @@ def test_reference_dispatch_spy_passes_on_engine(built):
         pytest.skip("reference tree absent and no prebuilt binary")
     r = subprocess.run([path], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr
+
+
+@pytest.mark.gpu
+def test_benchmark_cli_call_pattern(built, tmp_path):
+    """The reference CLI's sequence (tests/test_cohere_wiki_validation.cpp:
+    40-155): .bin loaders, graph-less cagra build, CGRA save/load, timed
+    searches, recall@10 against a float64 ground truth, dispatch spy."""
+    r = subprocess.run([os.path.join(built, "cli_test"), str(tmp_path)], capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "recall@10" in r.stdout
