@@ -152,11 +152,16 @@ int64_t knn_index_dim(const knn_index* index);
 int knn_index_copy_rows(knn_index* index, void* out, int dtype);
 
 /* Exact k-NN of n_queries fp32 queries (host or device, row-major, index
- * dim columns).  Writes neighbours (uint32) and squared distances (fp32),
- * each n_queries x k, ascending by (distance, index); slots beyond the
- * number of rows hold KNN_NO_INDEX / +inf.  Blocks until the results are in
- * place, like the reference (src/metal_context.mm:222-252).  k == 0 or
- * n_queries == 0 is a no-op.  When a communicator is attached
+ * dim columns), 1 <= k <= KNN_MAX_K.  Writes neighbours (uint32) and
+ * distances (fp32), each n_queries x k: squared L2 distances ascending by
+ * (distance, index), or for KNN_METRIC_INNER_PRODUCT the inner products
+ * descending (ties by ascending index); slots beyond the number of rows
+ * hold KNN_NO_INDEX / +inf (-inf for the inner product).  Blocks until the
+ * results are in place, like the reference (src/metal_context.mm:222-252).
+ * k == 0 or n_queries == 0 is a no-op.  Page-locked host buffers are read
+ * and written in place; pageable ones are staged through device memory.
+ * A search repeating the buffers and shape of an earlier one replays a CUDA
+ * graph (knn_index_set_graphs).  When a communicator is attached
  * (knn_index_attach_comm) every rank must call this with the same queries
  * and k; each rank receives the merged global result.
  * Replaces MetalContext::search_brute_force (src/metal_context.mm:139-255). */
