@@ -72,6 +72,20 @@ def test_dispatch_spy(engine, oracle_mod, torch_cuda):
     assert np.array_equal(d, g["distances"])
 
 
+def test_batching_l2_known_answer(engine, oracle_mod, torch_cuda):
+    """tests/test_benchmark_batching.py:220-239 of the reference: query e0
+    against e0, 2 e0 and e1 at D = 128 gives [0, 1, 2] exactly."""
+    dim = 128
+    query = np.zeros((1, dim), np.float32)
+    query[0, 0] = 1.0
+    cands = np.zeros((3, dim), np.float32)
+    cands[0, 0] = 1.0
+    cands[1, 0] = 2.0
+    cands[2, 1] = 1.0
+    i, d = _search(engine, cands, query, 3)
+    assert i.tolist() == [[0, 1, 2]] and d.tolist() == [[0.0, 1.0, 2.0]]
+
+
 def test_ties_duplicates_padding(engine, oracle_mod, torch_cuda):
     g = np.load(os.path.join(GOLDEN, "ties.npz"))
     i, d = _search(engine, g["base"], g["queries"], 45)
