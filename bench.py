@@ -18,6 +18,16 @@ Printed on rank 0, one JSON line:
   cpu_baseline the reference's own CPU exact search (oracle/_ref, compiled
                from its src/cagra.cpp) on a bounded sample of queries, all
                host threads; plus an OpenBLAS expanded-form port
+  latency      per-batch latency percentiles (nearest rank, as the
+               reference's cuvs_silicon/benchmark.py:573-578): end to end
+               through the blocking call with host buffers (host clock, as
+               tests/test_cohere_wiki_validation.cpp:165-185 times it) and
+               device-resident (CUDA events per search); max over ranks
+  parity       the merged result of the last end-to-end search (rank 0,
+               every GPU count) against the reference's own search on the
+               fp16-rounded rows, for a sample of the queries (acceptance
+               rule oracle.check_parity: indices equal or float64 distances
+               within rel 1e-3, recall 1, sorted, padding)
   clocks       SM clock samples (NVML) during the timed region
 
 --impl reference times the reference's CPU implementation alone (rank 0).
@@ -86,22 +96,29 @@ def peaks():
 
 
 def profile_traffic(a, n_shard):
-    """dram bytes per scan launch from the committed ncu summary, scaled to
-    this shard's rows when it was captured on a different row count."""
-    path = os.path.join(ROOT, "profiles", "knn_scan_headline.md")
+    """dram bytes per scan launch from the committed ncu figure
+    (profiles/knn_scan_traffic.json: dram__bytes_read.sum +
+    dram__bytes_write.sum of one captured launch), scaled to this shard's rows
+    when it was captured on a different row count (the scan's traffic grows
+    in proportion to the rows it reads)."""
+    path = os.path.join(ROOT, "profiles", "knn_scan_traffic.json")
     try:
-        vals = {}
-        for line in open(path):
-            if ":" in line and line.strip().startswith("- "):
-                key, _, v = line.strip()[2:].partition(":")
-                vals[key.strip()] = v.strip().split()[0]
-        t = float(vals["traffic_bytes_per_launch"])
-        rows = float(vals["captured_rows"])
-        if int(vals.get("captured_dim", a.dim)) != a.dim:
+        with open(path) as f:
+            v = json.load(f)
+        if int(v["captured_dim"]) != a.dim or int(v["captured_queries"]) < a.q // 2:
             return None
-        return t * n_shard / rows
+        return float(v["traffic_bytes_per_launch"]) * n_shard / float(v["captured_rows"])
     except Exception:
         return None
+
+
+def nearest_rank(values, pct):
+    """Nearest-rank percentile (the reference's cuvs_silicon/benchmark.py:573-578)."""
+    import math
+
+    v = sorted(values)
+    i = math.ceil(pct / 100.0 * len(v)) - 1
+    return v[max(0, min(i, len(v) - 1))]
 
 
 class ClockSampler:
@@ -261,7 +278,25 @@ def run_reference(a):
 
 
 # ---------------------------------------------------------------- engine arm
+def full_dataset_fp16_host(torch, a, centres, dev):
+    """The whole dataset, generated again on this GPU chunk by chunk with the
+    same per-chunk seeds every rank used for its shard, rounded to fp16 on
+    the device and returned as fp32 host rows (the values the engine
+    searches)."""
+    import numpy as np
+
+    out = np.empty((a.n, a.dim), dtype=np.float32)
+    step = 65536 * 4
+    for lo in range(0, a.n, step):
+        hi = min(a.n, lo + step)
+        x = gen_mixture_device(torch, a.n, lo, hi, a.dim, centres, 12, dev)
+        out[lo:hi] = x.half().float().cpu().numpy()
+        del x
+    return out
+
+
 def run_engine(a):
+    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -276,7 +311,7 @@ def run_engine(a):
     if world > 1:
         import datetime
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=dev)
 
     # ---- data (synthetic, on device)
@@ -302,11 +337,12 @@ def run_engine(a):
     metric = E.METRIC_INNER_PRODUCT if a.metric == "ip" else E.METRIC_L2_EXPANDED
     idx.build(shard, metric=metric, row_offset=lo, total_rows=a.n)
     torch.cuda.synchronize()
-    host_base16 = None
-    if rank == 0 and world == 1 and not a.no_cpu_baseline and a.metric == "l2":
+    host_base = None
+    check = rank == 0 and not a.no_cpu_baseline and a.metric == "l2"
+    if check and world == 1:
         # the rows the engine's results are exact for: fp16-rounded, or the
         # fp32 rows themselves with re-ranking
-        host_base16 = (shard if a.rerank else shard.half().float()).cpu().numpy()
+        host_base = (shard if a.rerank else shard.half().float()).cpu().numpy()
     del shard
     if world > 1:
         obj = [E.comm_unique_id() if rank == 0 else None]
@@ -324,27 +360,28 @@ def run_engine(a):
     def max_over_ranks(x):
         if world == 1:
             return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        t = torch.tensor(x if isinstance(x, list) else [x], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        v = t.cpu().tolist()
+        return v if isinstance(x, list) else v[0]
 
     # ---- warm-up
     for _ in range(a.warmup):
         idx.search_async(queries, a.k, out_i, out_d)
     idx.sync()
 
-    # ---- device-resident timing (value)
     clk = ClockSampler(local)
+    clk.__enter__()
+    # ---- device-resident timing (value)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     idx.reset_kernel_stats()
     barrier()
-    with clk:
-        ev0.record(stream)
-        for _ in range(a.steps):
-            idx.search_async(queries, a.k, out_i, out_d)
-        ev1.record(stream)
-        idx.sync()
-        torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(a.steps):
+        idx.search_async(queries, a.k, out_i, out_d)
+    ev1.record(stream)
+    idx.sync()
+    torch.cuda.synchronize()
     dev_ms = max_over_ranks(ev0.elapsed_time(ev1))
     launches = idx.kernel_stats()["kernel_launches"]
     launches_total = int(max_over_ranks(float(launches)) * world)
@@ -362,6 +399,19 @@ def run_engine(a):
     scan_ms = max_over_ranks(st["scan_ms"] / max(1, st["scan_launches"]))
     merge_ms = max_over_ranks(st["merge_ms"] / max(1, st["scan_launches"]))
 
+    # ---- device-resident latency: one search at a time, events around each
+    lat_dev = []
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(a.steps)]
+    barrier()
+    for e0, e1 in evs:
+        e0.record(stream)
+        idx.search_async(queries, a.k, out_i, out_d)
+        e1.record(stream)
+        idx.sync()
+    torch.cuda.synchronize()
+    lat_dev = max_over_ranks([e0.elapsed_time(e1) for e0, e1 in evs])
+
     # ---- end-to-end through the public API with pinned host buffers
     q_host = queries.cpu().pin_memory()
     i_host = torch.empty((a.q, a.k), dtype=torch.int32).pin_memory()
@@ -377,35 +427,85 @@ def run_engine(a):
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     e2e = a.q * a.steps / (e2e_ms / 1000.0)
+    # per-batch wall-clock latency of the blocking call (the reference's
+    # benchmark times each cagra::search call with a host clock)
+    lat_e2e = []
+    barrier()
+    for _ in range(a.steps):
+        t0 = time.perf_counter()
+        idx.search(q_host, a.k, neighbors=i_host, distances=d_host)
+        lat_e2e.append(1000.0 * (time.perf_counter() - t0))
+    lat_e2e = max_over_ranks(lat_e2e)
+    clk.__exit__(None, None, None)
     gpu_nbrs = i_host.numpy().view("uint32").copy()
+    gpu_dists = d_host.numpy().copy()
 
-    # ---- CPU baselines (rank 0, N = 1 only; bounded samples)
+    # every rank holds the merged global result: do they agree?
+    ranks_agree = True
+    if world > 1:
+        mine = torch.from_numpy(np.concatenate([gpu_nbrs.view(np.int32).ravel(),
+                                                gpu_dists.view(np.int32).ravel()])).to(dev)
+        allr = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allr, mine)
+        ranks_agree = all(bool(torch.equal(allr[0], t)) for t in allr)
+
+    # ---- CPU baselines (rank 0, N = 1 only; bounded samples) and parity
+    # (rank 0, every N)
     cpu = None
     extra = {}
-    if host_base16 is not None:
+    parity = None
+    if check:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+
         threads = host_threads()
         q16 = (queries if a.rerank else queries.half().float()).cpu().numpy()
-        sample = max(1, min(a.q, 2 * threads))
-        qps, secs, ref_i, ref_d, kind = cpu_reference_qps(host_base16, q16, a.k, sample, threads)
-        cpu = {"value": qps, "unit": UNIT, "cores": min(threads, sample), "kind": kind,
-               "sample": f"{sample} of {a.q} queries against all {a.n} rows "
-                         f"({secs:.1f} s, reference cagra::search, one query slice per thread)"}
-        hits = sum(len(set(x.tolist()) & set(y.tolist()))
-                   for x, y in zip(gpu_nbrs[:sample], ref_i))
-        extra["recall_vs_reference_sample"] = hits / float(ref_i.size)
-        try:
-            sys.path.insert(0, os.path.join(ROOT, "oracle"))
-            import oracle
-
+        if world == 1:
+            sample = max(1, min(a.q, 2 * threads))
+            qps, secs, ref_i, ref_d, kind = cpu_reference_qps(host_base, q16, a.k, sample,
+                                                              threads)
+            cpu = {"value": qps, "unit": UNIT, "cores": min(threads, sample), "kind": kind,
+                   "sample": f"{sample} of {a.q} queries against all {a.n} rows "
+                             f"({secs:.1f} s, reference cagra::search, one query slice "
+                             f"per thread)"}
+            try:
+                t0 = time.perf_counter()
+                oracle.blas_knn(host_base, q16, a.k)
+                bt = time.perf_counter() - t0
+                extra["cpu_blas_expanded_form"] = {
+                    "value": a.q / bt, "unit": UNIT, "cores": threads, "kind": "port",
+                    "sample": f"all {a.q} queries, numpy float32 matmul "
+                              f"(OpenBLAS sgemm, {oracle.blas_threads()}), {bt:.1f} s"}
+            except Exception as e:  # informational only
+                extra["cpu_blas_expanded_form"] = {"error": str(e)[:200]}
+        else:
+            # the merged multi-rank result against the whole dataset, which
+            # no rank holds: regenerate it here
             t0 = time.perf_counter()
-            oracle.blas_knn(host_base16, q16, a.k)
-            bt = time.perf_counter() - t0
-            extra["cpu_blas_expanded_form"] = {
-                "value": a.q / bt, "unit": UNIT, "cores": threads, "kind": "port",
-                "sample": f"all {a.q} queries, numpy float32 matmul "
-                          f"(OpenBLAS sgemm, {oracle.blas_threads()}), {bt:.1f} s"}
-        except Exception as e:  # informational only
-            extra["cpu_blas_expanded_form"] = {"error": str(e)[:200]}
+            host_base = full_dataset_fp16_host(torch, a, centres, dev)
+            sample = max(1, min(a.q, 16))
+            _, secs, ref_i, ref_d, kind = cpu_reference_qps(host_base, q16, a.k, sample,
+                                                            threads)
+            secs = time.perf_counter() - t0
+        par = (oracle.check_parity(host_base, q16[:sample], gpu_nbrs[:sample],
+                                   gpu_dists[:sample], ref_i, ref_d, 1e-3)
+               if not a.rerank else None)
+        exact = (bool(np.array_equal(gpu_nbrs[:sample], ref_i)
+                      and np.array_equal(gpu_dists[:sample], ref_d)) if a.rerank else None)
+        parity = {
+            "ok": bool(par.ok if par is not None else exact) and ranks_agree,
+            "queries_checked": sample, "of": a.q,
+            "oracle": ("reference cagra::search (oracle/_ref, the reference's "
+                       "src/cagra.cpp compiled unmodified)" if kind == "reference"
+                       else "C restatement of src/cagra.cpp:211-252 (oracle/knn_oracle.c)"),
+            "rule": ("byte-identical to the reference's fp32 search" if a.rerank else
+                     "oracle.check_parity on fp16-rounded rows: index equal or float64 "
+                     "distances within rel 1e-3; recall@k 1.0; sorted; padding"),
+            "detail": par.detail if par is not None else f"identical={exact}",
+            "ranks_agree": ranks_agree,
+            "result_of": f"the last end-to-end search, merged over {world} rank(s)",
+        }
+        del host_base
 
     n_shard = hi - lo
     peak, peak_kind = peaks()
@@ -428,7 +528,9 @@ def run_engine(a):
                            " + NVLink peer exchange of the per-rank top-k lists"
                            if world > 1 else ""),
                        "l2": f"inputs larger than L2 (dataset shard {shard_mb:.0f} MiB "
-                             f"> 126 MiB), no flush"},
+                             f"> 126 MiB), no flush" if shard_mb > 126 else
+                             f"dataset shard {shard_mb:.0f} MiB fits in the 126 MiB L2 "
+                             f"(no flush): not an HBM measurement"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_kind": peak_kind, "kernel": "knn_scan_kernel",
@@ -437,6 +539,15 @@ def run_engine(a):
             "cpu_baseline": cpu,
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": a.q * a.dim * 4,
                     "d2h_bytes_per_step": a.q * a.k * 8},
+            "latency": {
+                "e2e_p50_ms": nearest_rank(lat_e2e, 50), "e2e_p99_ms": nearest_rank(lat_e2e, 99),
+                "device_p50_ms": nearest_rank(lat_dev, 50),
+                "device_p99_ms": nearest_rank(lat_dev, 99),
+                "samples": a.steps,
+                "how": "one batch at a time; e2e = host clock around the blocking search "
+                       "with pinned host buffers; device = CUDA events around one "
+                       "device-resident search; max over ranks per sample; nearest rank"},
+            "parity": parity,
             "gpu_launches": launches_total,
             "clocks": clk.summary(),
         }

@@ -252,7 +252,8 @@ struct knn_index {
   float* xbuf = nullptr;
   float* xpeer[knn::kMaxRanks] = {};
   int64_t xcap = 0;
-  uint32_t epoch = 0;
+  uint32_t* epoch_dev = nullptr;  // the exchange epoch (see knn::Exchange)
+  uint64_t peer_wait_ns = knn::kPeerWaitDefaultNs;
 
   // CUDA graphs of the device-side search pipeline, replayed when a search
   // repeats the buffers and shape of a captured one.  `generation` changes
@@ -334,6 +335,8 @@ int setup_exchange(knn_index* h) {
   std::memset(&mine, 0, sizeof(mine));
   bool ok = cudaMalloc(&h->xbuf, static_cast<size_t>(words) * 4) == cudaSuccess;
   if (ok) ok = cudaMemset(h->xbuf, 0, static_cast<size_t>(words) * 4) == cudaSuccess;
+  if (ok) ok = cudaMalloc(&h->epoch_dev, sizeof(uint32_t)) == cudaSuccess;
+  if (ok) ok = cudaMemset(h->epoch_dev, 0, sizeof(uint32_t)) == cudaSuccess;
   if (ok) ok = cudaIpcGetMemHandle(&mine, h->xbuf) == cudaSuccess;
   cudaGetLastError();
   // every rank takes part in the all-gather, even with a failed allocation
@@ -409,7 +412,6 @@ int setup_exchange(knn_index* h) {
     return KNN_OK;
   }
   h->xcap = kExchangeCapQK;
-  h->epoch = 0;
   return KNN_OK;
 }
 
@@ -448,7 +450,9 @@ void drop_exchange(knn_index* h) {
     h->xpeer[r] = nullptr;
   }
   if (h->xbuf) cudaFree(h->xbuf);
+  if (h->epoch_dev) cudaFree(h->epoch_dev);
   h->xbuf = nullptr;
+  h->epoch_dev = nullptr;
   h->xcap = 0;
 }
 
@@ -497,8 +501,10 @@ int check_device_error(knn_index* h) {
     cudaStreamSynchronize(h->stream);
     if (code == knn::kErrTimeoutPeer)
       return fail(KNN_ETIMEOUT,
-                  "a peer's list did not arrive within the 1 s bound (device code %d); "
-                  "attach the communicator again before the next search", code);
+                  "a peer's list did not arrive within %.3f s of this rank's own (device "
+                  "code %d): every rank must issue each search within that bound "
+                  "(knn_index_set_peer_timeout); attach the communicator again before the "
+                  "next search", static_cast<double>(h->peer_wait_ns) * 1e-9, code);
     return fail(KNN_ETIMEOUT, "scan kernel gave up on a bounded wait (device code %d)", code);
   }
   return KNN_OK;
@@ -518,6 +524,12 @@ int validate_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
   return KNN_OK;
 }
 
+// Whether a search of nq queries x k on an index with a communicator
+// exchanges its lists through the NVLink peer buffers (else NCCL).
+bool uses_peer_exchange(const knn_index* h, int64_t nq, int64_t k) {
+  return h->comm && h->peer_enabled && h->xcap > 0 && h->epoch_dev && nq * k <= h->xcap;
+}
+
 // Everything a search enqueues on the device between the query upload and
 // the result download: query conversion, scan, merge(s) and the all-gather.
 // Captured into a CUDA graph when the search is replayable.
@@ -534,7 +546,7 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
   if (rerank) KNN_CUDA(cudaMemsetAsync(h->uncert_dev, 0, sizeof(int), h->stream));
   KNN_CUDA(knn::launch_convert_rows(qsrc, false, nq, nq_pad, h->dim, h->q16.as<__half>(),
                                     h->ld, h->qnorm.as<float>(), h->stream,
-                                    h->bound.as<uint32_t>(), nq));
+                                    h->bound.as<uint32_t>(), nq, h->epoch_dev));
   CUtensorMap qmap;
   if ((st = encode_rows(&qmap, h->q16.as<__half>(), nq_pad, h->ld, knn::kQueryRows)) != KNN_OK)
     return st;
@@ -624,7 +636,7 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
     KNN_CUDA(knn::launch_merge(ld, li, l_stride, q_stride, n_lists, static_cast<int>(k), nq,
                                off, dst_d, dst_i, out_i64, h->stream, overlap, nullptr, neg));
     launches += 1;
-  } else if (h->peer_enabled && h->xcap > 0 && static_cast<int64_t>(qk) <= h->xcap) {
+  } else if (uses_peer_exchange(h, nq, k)) {
     // peer exchange: the local merge writes every query's list into every
     // rank's exchange buffer over NVLink as epoch-tagged words; the final
     // merge collects them from its own buffer (bounded wait) and merges
@@ -633,8 +645,8 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
     ex.cap_qk = h->xcap;
     ex.n_ranks = h->n_ranks;
     ex.rank = h->rank;
-    ex.epoch = ++h->epoch;
-    ex.parity = static_cast<int>(ex.epoch & 1u);
+    ex.epoch = h->epoch_dev;
+    ex.wait_ns = h->peer_wait_ns;
     ex.err = h->err_dev;
     ex.mode = 1;
     KNN_CUDA(knn::launch_merge(ld, li, l_stride, q_stride, n_lists, static_cast<int>(k), nq, off,
@@ -758,10 +770,12 @@ int search_pass(knn_index* h, const float* queries, int64_t nq, int64_t k, int64
   // Replay a graph for searches that repeat buffers + shape.  Host buffers
   // qualify too: the graph reads and writes either them in place (page-
   // locked, part of the key) or the staging buffers (whose reallocation
-  // bumps the generation).  Not with a communicator: replaying the captured
-  // all-gather measured slower than launching it directly (8 ranks on one
-  // NVSwitch node).
-  const bool graphable = h->use_graphs && !prof && !h->comm;
+  // bumps the generation).  With a communicator only the peer exchange is
+  // replayed (its epoch lives in device memory, so its kernels take the same
+  // arguments every search); the NCCL all-gather path is launched directly
+  // (replaying the captured all-gather measured slower at 8 ranks).
+  const bool graphable =
+      h->use_graphs && !prof && (!h->comm || uses_peer_exchange(h, nq, k));
   knn_index::GraphEntry* hit = nullptr;
   if (graphable) {
     for (auto& g : h->graphs) {
@@ -1437,7 +1451,23 @@ int knn_index_attach_comm(knn_index* h, const void* uid, int n_ranks, int rank) 
 int knn_index_set_peer_exchange(knn_index* h, int enabled) {
   if (!h) return fail(KNN_EINVAL, "null index");
   std::lock_guard<std::mutex> lock(h->mu);
+  KNN_CUDA(cudaSetDevice(h->device));
   h->peer_enabled = enabled != 0;
+  ++h->generation;
+  drop_graphs(h);
+  return KNN_OK;
+}
+
+int knn_index_set_peer_timeout(knn_index* h, int64_t microseconds) {
+  if (!h) return fail(KNN_EINVAL, "null index");
+  if (microseconds < 1000 || microseconds > 600000000)
+    return fail(KNN_EINVAL, "peer timeout %lld us outside [1 ms, 600 s]",
+                (long long)microseconds);
+  std::lock_guard<std::mutex> lock(h->mu);
+  KNN_CUDA(cudaSetDevice(h->device));
+  h->peer_wait_ns = static_cast<uint64_t>(microseconds) * 1000u;
+  ++h->generation;  // the bound is a kernel argument of captured searches
+  drop_graphs(h);
   return KNN_OK;
 }
 

@@ -87,11 +87,13 @@ cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
 // fp32 norms of the rounded rows.  in_is_half selects the input type.
 // Output rows [rows, rows_out) are written as zeros (no norm).  fill
 // (optional): fill_n words set to 0xFFFFFFFF (the scan's shared per-query
-// bounds, reset by the query conversion of every search).
+// bounds, reset by the query conversion of every search).  epoch (optional):
+// a device word incremented once (the exchange epoch of the search that this
+// conversion opens).
 cudaError_t launch_convert_rows(const void* in, bool in_is_half, int64_t rows,
                                 int64_t rows_out, int64_t dim, __half* out, int64_t ld,
                                 float* norms, cudaStream_t stream, uint32_t* fill = nullptr,
-                                int64_t fill_n = 0);
+                                int64_t fill_n = 0, uint32_t* epoch = nullptr);
 
 // Rows of the fp16 query buffer a search needs: every 128-row query slab
 // the scan kernel loads lies inside it, so no TMA box leaves the buffer.
@@ -112,20 +114,28 @@ cudaError_t launch_bounded_wait_selftest(int* err, uint64_t limit_ns, cudaStream
 // `base[r]` is rank r's buffer as this GPU addresses it (its own allocation
 // or a CUDA IPC mapping).  Searches alternate parities, so a rank can write
 // search e + 1 while a slower peer still reads search e.
+//
+// The epoch lives in device memory (`epoch`), not in the kernel arguments:
+// the query conversion that opens every search adds one to it (after waiting
+// for the previous search's kernels), and both exchange kernels read it only
+// after their own griddepcontrol.wait, by which time that conversion has
+// completed.  A search's kernels therefore carry no per-search argument and
+// can be captured once in a CUDA graph and replayed.
 constexpr int kMaxRanks = 8;
 struct Exchange {
   float* base[kMaxRanks];
   int64_t cap_qk;
   int n_ranks;
   int rank;
-  int mode;        // 0 none; 1 push this rank's lists to every rank; 2 receive and merge
-  uint32_t epoch;  // increases by one per search (never 0)
-  int parity;      // epoch & 1: which half this search uses
-  int* err;        // device error word (wait timeouts)
-  float* dec_d;    // mode 2: received lists, decoded: [q][n_ranks][k]
+  int mode;               // 0 none; 1 push this rank's lists to every rank; 2 receive and merge
+  const uint32_t* epoch;  // device word: the current search's epoch (>= 1)
+  uint64_t wait_ns;       // mode 2: how long to wait for a peer's list
+  int* err;               // device error word (wait timeouts)
+  float* dec_d;           // mode 2: received lists, decoded: [q][n_ranks][k]
   uint32_t* dec_i;
 };
 constexpr int kErrTimeoutPeer = 7;  // a peer's list never arrived
+constexpr uint64_t kPeerWaitDefaultNs = 1000000000ull;  // 1 s
 
 inline int64_t exchange_words(int n_ranks, int64_t cap_qk) {
   return static_cast<int64_t>(n_ranks) * cap_qk * 8;  // 2 parities x 16 bytes, in 4-byte words

@@ -273,35 +273,44 @@ __device__ __forceinline__ void st_relaxed_sys_v2(uint64_t* p, uint64_t a, uint6
 }
 
 // Mode 2: the block collects every rank's list for query q from this
-// rank's exchange buffer, waiting (bounded, 1 s) until both words of each
-// entry carry this search's epoch, and decodes them to ex.dec_d/dec_i.
-// Returns false (for the whole block) after recording kErrTimeoutPeer when
-// an entry never arrives.
-__device__ bool receive_lists(const Exchange& ex, int64_t q, int k, int* s_abort) {
+// rank's exchange buffer, waiting (bounded by ex.wait_ns) until both words of
+// each entry carry this search's epoch, and decodes them to ex.dec_d/dec_i.
+// Returns false (for the whole block) after recording kErrTimeoutPeer when an
+// entry never arrives, or as soon as another block has recorded an error
+// (so a missing peer costs one bound, not one bound per wave of blocks).
+__device__ bool receive_lists(const Exchange& ex, uint32_t epoch, int64_t q, int k,
+                              int* s_abort) {
   if (threadIdx.x == 0) *s_abort = 0;
   __syncthreads();
   const uint64_t* own = reinterpret_cast<const uint64_t*>(ex.base[ex.rank]);
+  const int parity = static_cast<int>(epoch & 1u);
   const int total = ex.n_ranks * k;
   for (int i = threadIdx.x; i < total; i += blockDim.x) {
     const int r = i / k;
     const int e = i - r * k;
     const uint64_t* src =
-        own + ((static_cast<int64_t>(ex.parity) * ex.n_ranks + r) * ex.cap_qk + q * k + e) * 2;
+        own + ((static_cast<int64_t>(parity) * ex.n_ranks + r) * ex.cap_qk + q * k + e) * 2;
     uint64_t a, b;
     uint64_t t0 = 0;
+    uint32_t spins = 0;
     bool ok = true;
     while (true) {
       ld_relaxed_sys_v2(src, a, b);
-      if (static_cast<uint32_t>(a >> 32) == ex.epoch && static_cast<uint32_t>(b >> 32) == ex.epoch)
+      if (static_cast<uint32_t>(a >> 32) == epoch && static_cast<uint32_t>(b >> 32) == epoch)
         break;
       if (*reinterpret_cast<volatile int*>(s_abort)) {
+        ok = false;
+        break;
+      }
+      if ((++spins & 31u) == 0 && *reinterpret_cast<volatile int*>(ex.err) != 0) {
+        *reinterpret_cast<volatile int*>(s_abort) = 1;
         ok = false;
         break;
       }
       uint64_t now;
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
       if (t0 == 0) t0 = now;
-      if (now - t0 > 1000000000ull) {
+      if (now - t0 > ex.wait_ns) {
         atomicCAS(ex.err, 0, kErrTimeoutPeer);
         *reinterpret_cast<volatile int*>(s_abort) = 1;
         ok = false;
@@ -320,9 +329,9 @@ __device__ bool receive_lists(const Exchange& ex, int64_t q, int k, int* s_abort
 // rest padding) to the output, or in mode 1 to every rank's exchange buffer
 // as epoch-tagged words.  Called by every thread of the block.
 template <typename OutIdx>
-__device__ void emit_result(const Exchange& ex, int64_t q, int k, const float* rd,
-                            const uint32_t* ri, int count, int64_t index_offset, float* out_d,
-                            OutIdx* out_i, float sign) {
+__device__ void emit_result(const Exchange& ex, uint32_t epoch, int64_t q, int k,
+                            const float* rd, const uint32_t* ri, int count,
+                            int64_t index_offset, float* out_d, OutIdx* out_i, float sign) {
   const float kInf = __int_as_float(0x7f800000);
   if (ex.mode != 1) {
     for (int e = threadIdx.x; e < k; e += blockDim.x) {
@@ -332,8 +341,9 @@ __device__ void emit_result(const Exchange& ex, int64_t q, int k, const float* r
     }
     return;
   }
-  const uint64_t tag = static_cast<uint64_t>(ex.epoch) << 32;
-  const int64_t at = ((static_cast<int64_t>(ex.parity) * ex.n_ranks + ex.rank) * ex.cap_qk + q * k);
+  const uint64_t tag = static_cast<uint64_t>(epoch) << 32;
+  const int64_t parity = static_cast<int64_t>(epoch & 1u);
+  const int64_t at = ((parity * ex.n_ranks + ex.rank) * ex.cap_qk + q * k);
   for (int e = threadIdx.x; e < k; e += blockDim.x) {
     const bool have = e < count;
     const uint32_t idx = have ? ri[e] : kNoIndex;
@@ -353,7 +363,7 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
                                             int n_lists, int k, int64_t index_offset,
                                             float* __restrict__ out_d,
                                             OutIdx* __restrict__ out_i, const Exchange& ex,
-                                            float sign) {
+                                            uint32_t epoch, float sign) {
   extern __shared__ uint8_t smem_raw[];
   float* sd = reinterpret_cast<float*>(smem_raw);
   uint32_t* si = reinterpret_cast<uint32_t*>(sd + kStageEntries);
@@ -376,7 +386,7 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
   if (n_lists > kSelCap) {
     fold_merge<E>(sd, si, qd, qi, stride_list, n_lists, k, sd + kSelCap, si + kSelCap);
     __syncthreads();
-    emit_result(ex, q, k, sd + kSelCap, si + kSelCap, k, index_offset, out_d, out_i, sign);
+    emit_result(ex, epoch, q, k, sd + kSelCap, si + kSelCap, k, index_offset, out_d, out_i, sign);
     return;
   }
   int p2 = 1;
@@ -499,14 +509,14 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
     __syncthreads();
     fold_merge<E>(sd, si, qd, qi, stride_list, n_lists, k, cd, ci);
     __syncthreads();
-    emit_result(ex, q, k, cd, ci, k, index_offset, out_d, out_i, sign);
+    emit_result(ex, epoch, q, k, cd, ci, k, index_offset, out_d, out_i, sign);
     return;
   }
   if (count <= kRankPlaceMax) {
     // candidates are distinct (distinct row indices): rank counting places
     // the first k of them, sorted, in front of the selection array
     rank_place(cd, ci, count, seld, seli, k);
-    emit_result(ex, q, k, seld, seli, count, index_offset, out_d, out_i, sign);
+    emit_result(ex, epoch, q, k, seld, seli, count, index_offset, out_d, out_i, sign);
     return;
   }
   int c2 = 1;
@@ -517,7 +527,7 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
   }
   __syncthreads();
   block_sort(cd, ci, c2);
-  emit_result(ex, q, k, cd, ci, count, index_offset, out_d, out_i, sign);
+  emit_result(ex, epoch, q, k, cd, ci, count, index_offset, out_d, out_i, sign);
 }
 
 template <int E, typename OutIdx>
@@ -531,20 +541,20 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ int s_abort;
   const int64_t q = blockIdx.x;
+  // Everything this kernel reads was written by kernels before it in the
+  // stream; in particular the exchange epoch, which the query conversion
+  // that opened this search incremented.  Mode 2 waits for the local merge
+  // (mode 1) of this rank too, whose stores carry this rank's own list.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const uint32_t epoch = ex.mode != 0 ? *reinterpret_cast<const volatile uint32_t*>(ex.epoch) : 0u;
   if (ex.mode == 2) {
-    // The input arrives through this rank's exchange buffer, tagged with the
-    // search's epoch, so the block starts without waiting for the local
-    // merge before it.  It waits at its end instead: this kernel then
-    // completes only after that one, as stream order requires.
-    if (receive_lists(ex, q, k, &s_abort))
+    if (receive_lists(ex, epoch, q, k, &s_abort))
       merge_query<E, OutIdx>(in_d, in_i, stride_list, stride_query, n_lists, k, index_offset,
-                             out_d, out_i, ex, sign);
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+                             out_d, out_i, ex, epoch, sign);
     return;
   }
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   merge_query<E, OutIdx>(in_d, in_i, stride_list, stride_query, n_lists, k, index_offset, out_d,
-                         out_i, ex, sign);
+                         out_i, ex, epoch, sign);
 }
 
 template <int E>

@@ -38,14 +38,18 @@ template <bool kHalfIn>
 __global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, int64_t rows_out,
                                     int64_t dim, __half* __restrict__ out, int64_t ld,
                                     float* __restrict__ norms, bool vec,
-                                    uint32_t* __restrict__ fill, int64_t fill_n) {
+                                    uint32_t* __restrict__ fill, int64_t fill_n,
+                                    uint32_t* __restrict__ epoch) {
   // Let the next kernel (the scan) be scheduled now: its dataset loads do
   // not depend on this kernel, and it waits before reading the queries.
   // This kernel is itself a programmatic dependent of the previous search's
   // kernels, which may still read `out`: wait for them before writing.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  // per-search state of the scan that follows (its shared per-query bounds)
+  // per-search state: the exchange epoch (read by the merge kernels of this
+  // search after their own griddepcontrol.wait) and the scan's shared
+  // per-query bounds
+  if (epoch && blockIdx.x == 0 && threadIdx.x == 0) *epoch += 1u;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < fill_n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     fill[i] = 0xFFFFFFFFu;
@@ -116,7 +120,8 @@ __global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, i
 
 cudaError_t launch_convert_rows(const void* in, bool in_is_half, int64_t rows, int64_t rows_out,
                                 int64_t dim, __half* out, int64_t ld, float* norms,
-                                cudaStream_t stream, uint32_t* fill, int64_t fill_n) {
+                                cudaStream_t stream, uint32_t* fill, int64_t fill_n,
+                                uint32_t* epoch) {
   if (rows_out < rows) rows_out = rows;
   if (rows_out <= 0) return cudaSuccess;
   const bool vec = (dim % 8 == 0) && ((reinterpret_cast<uintptr_t>(in) & 15u) == 0) &&
@@ -136,9 +141,9 @@ cudaError_t launch_convert_rows(const void* in, bool in_is_half, int64_t rows, i
   cfg.numAttrs = 1;
   if (in_is_half)
     return cudaLaunchKernelEx(&cfg, convert_rows_kernel<true>, in, rows, rows_out, dim, out, ld,
-                              norms, vec, fill, fill ? fill_n : int64_t(0));
+                              norms, vec, fill, fill ? fill_n : int64_t(0), epoch);
   return cudaLaunchKernelEx(&cfg, convert_rows_kernel<false>, in, rows, rows_out, dim, out, ld,
-                            norms, vec, fill, fill ? fill_n : int64_t(0));
+                            norms, vec, fill, fill ? fill_n : int64_t(0), epoch);
 }
 
 }  // namespace knn

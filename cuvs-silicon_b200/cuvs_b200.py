@@ -86,6 +86,7 @@ def lib() -> ctypes.CDLL:
         "knn_index_set_profiling": (I, [P, I]),
         "knn_index_set_graphs": (I, [P, I]),
         "knn_index_set_peer_exchange": (I, [P, I]),
+        "knn_index_set_peer_timeout": (I, [P, I64]),
         "knn_index_kernel_stats": (I, [P, ctypes.POINTER(ctypes.c_double),
                                        ctypes.POINTER(ctypes.c_double),
                                        ctypes.POINTER(I64), ctypes.POINTER(I64)]),
@@ -296,6 +297,11 @@ class Index:
 
     def set_peer_exchange(self, on: bool) -> None:
         _check(lib().knn_index_set_peer_exchange(self._h, 1 if on else 0))
+
+    def set_peer_timeout(self, seconds: float) -> None:
+        """Bound of the peer-exchange wait (every rank must issue each search
+        within it of the others; see knn_index_set_peer_timeout)."""
+        _check(lib().knn_index_set_peer_timeout(self._h, int(round(seconds * 1e6))))
 
     def set_graphs(self, on: bool) -> None:
         _check(lib().knn_index_set_graphs(self._h, 1 if on else 0))

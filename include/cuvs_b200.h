@@ -191,7 +191,15 @@ int knn_index_search_i64(knn_index* index, const float* queries,
  * device address, so make it before any stream capture.  Calls share the
  * array: concurrent calls on one device are serialised by the library; other
  * work that overlaps them on the GPU and touches the array would race.
- * The index must be built, and no communicator may be attached. */
+ * The index must be built, and no communicator may be attached.  Unlike
+ * knn_index_search it runs neither the pilot pass (k >= 17) nor the
+ * per-query bound the scan's CTAs share, whose scratch it does not carve:
+ * results are the same, but searches with k >= 17 run the slower unseeded
+ * scan (k = 256 at 1M x 1024 took 2.5-3.4x as long before the engine had
+ * these two steps).  The array's device address is
+ * cached per device for the life of the process; a device reset
+ * (cudaDeviceReset), which also invalidates every index on that device, is
+ * not supported. */
 int knn_index_search_noalloc(knn_index* index, const float* queries,
                              int64_t n_queries, int64_t k, uint32_t* neighbors,
                              float* distances);
@@ -260,25 +268,35 @@ int knn_comm_unique_id(void* out_128_bytes);
 int knn_index_attach_comm(knn_index* index, const void* unique_id_128_bytes,
                           int n_ranks, int rank);
 
-/* CUDA graphs (on by default): a search whose queries and outputs are all
- * device memory is captured once into a CUDA graph (query conversion, scan,
- * merge and, with a communicator, the all-gather and final merge) and
- * replayed when later searches repeat the same buffers, sizes and stream.
- * Rebuilding the index, changing its stream or communicator, or growing its
- * scratch memory discards the graphs.  Searches on an index with a
- * communicator attached are always launched directly.  No counterpart in
- * the reference. */
+/* CUDA graphs (on by default): a search is captured once into a CUDA graph
+ * (query conversion, scan, merges and, with a communicator, the peer
+ * exchange) and replayed when later searches repeat the same buffers, sizes
+ * and stream.  Rebuilding the index, changing its stream, communicator,
+ * peer-exchange setting or peer timeout, or growing its scratch memory
+ * discards the graphs.  Searches that exchange their lists through NCCL
+ * (see knn_index_set_peer_exchange) are always launched directly.  No
+ * counterpart in the reference. */
 int knn_index_set_graphs(knn_index* index, int enabled);
 
 /* Peer exchange (on by default when every rank could map every other
  * rank's exchange buffer at knn_index_attach_comm): the per-rank top-k
  * lists of a search travel as direct NVLink stores into every rank's
- * buffer, each query's list followed by an epoch flag, and the final merge
- * waits (bounded, 1 s) for the flags.  Searches with more than 65,536
- * query x k entries, and indexes with the exchange off, use the NCCL
- * all-gather.  Every rank must make the same choice.  No counterpart in the
- * reference. */
+ * buffer, every entry tagged with the search's epoch, and each rank's final
+ * merge waits for its peers' entries for at most the peer timeout (below),
+ * counted from the moment this rank's own lists are complete.  Searches
+ * with more than 65,536 query x k entries, and indexes with the exchange
+ * off, use the NCCL all-gather.  Every rank must make the same choice.  No
+ * counterpart in the reference. */
 int knn_index_set_peer_exchange(knn_index* index, int enabled);
+
+/* Bound of the peer-exchange wait, in microseconds (1 ms .. 600 s; default
+ * 1 s).  Every rank must issue each search within this bound of the others
+ * (the slowest rank's lists must arrive before the fastest rank's wait
+ * runs out): host-side skew between ranks (Python, first-call set-up, a
+ * rank that computes something else first) counts against it.  When the
+ * bound expires the search returns KNN_ETIMEOUT and the communicator must
+ * be attached again.  No counterpart in the reference. */
+int knn_index_set_peer_timeout(knn_index* index, int64_t microseconds);
 
 /* Kernel timing: when enabled, the engine records CUDA events around its
  * fused scan kernel and its merge kernels on the stream they are launched on

@@ -10,7 +10,9 @@ torch.distributed.run).  Modes:
               instead of hanging.
   gpu         one GPU per rank: row shards built with global offsets,
               NCCL communicator attached, every rank searches and receives
-              the merged global result, checked against the oracle.
+              the merged global result, checked against the oracle;
+              graph-replayed peer-exchange searches, a 200 ms skew between
+              the ranks, and a missing peer (bounded wait, KNN_ETIMEOUT).
   gpu-exact   one GPU per rank: exact fp32 re-ranking on every shard (the
               merged result must equal the oracle on the unrounded rows
               byte for byte) and the inner-product metric, through the
@@ -20,6 +22,7 @@ Exit code 0 = pass.
 import datetime
 import os
 import sys
+import time
 
 import numpy as np
 
@@ -87,15 +90,26 @@ def main():
                 oi, od = O.port_knn(b16, q16, k, threads=4)
                 par = O.check_parity(b16, q16, gi, gd, oi, od, 1e-3)
                 assert par.ok, f"rank {rank} k={k}: {par.detail}"
-            # stream-ordered path with device buffers, twice
+            # stream-ordered path with device buffers: the first search runs
+            # directly, the second is captured into a CUDA graph, the rest
+            # replay it (the exchange epoch advances on the device)
             qd = torch.from_numpy(queries).cuda()
             ni = torch.empty((nq, 10), dtype=torch.int32, device="cuda")
             nd = torch.empty((nq, 10), dtype=torch.float32, device="cuda")
             ref_i, ref_d = idx.search(queries, 10)
-            for _ in range(2):
+            for _ in range(5):
+                ni.zero_()
                 idx.search_async(qd, 10, ni, nd)
                 idx.sync()
                 assert np.array_equal(ni.cpu().numpy().view(np.uint32), ref_i)
+                assert np.array_equal(nd.cpu().numpy(), ref_d)
+            # host-side skew between ranks within the peer timeout: rank 1
+            # issues its search 200 ms after rank 0
+            dist.barrier()
+            if rank == 1:
+                time.sleep(0.2)
+            gi, gd = idx.search(queries, 10)
+            assert np.array_equal(gi, ref_i) and np.array_equal(gd, ref_d)
             # the NCCL all-gather fallback gives the same bytes
             idx.set_peer_exchange(False)
             gi, gd = idx.search(queries, 10)
@@ -106,15 +120,25 @@ def main():
             dist.barrier()
             # failure detection: rank 1 skips this search, so rank 0's final
             # merge waits for lists that never come; its bounded wait must
-            # give up and report KNN_ETIMEOUT (the GPU stays usable)
+            # give up and report KNN_ETIMEOUT (the GPU stays usable).  2,048
+            # queries make several waves of merge blocks: once one block has
+            # recorded the timeout the others give up at once, so the error
+            # comes back after about one bound, not one bound per wave.
+            many = O.gen_iid(2048, dim, 103)
+            idx.set_peer_timeout(0.5)
+            dist.barrier()
             if rank == 0:
+                t0 = time.perf_counter()
                 try:
-                    idx.search(queries, 10)
+                    idx.search(many, 10)
                     print("rank 0: search without its peer did not time out", flush=True)
                     return 1
                 except RuntimeError as e:
+                    waited = time.perf_counter() - t0
                     assert "ETIMEOUT" in str(e), str(e)
-                    print("rank 0 detected the missing peer list", flush=True)
+                    assert waited < 1.5, f"timeout took {waited:.2f} s for a 0.5 s bound"
+                    print(f"rank 0 detected the missing peer list after {waited:.2f} s",
+                          flush=True)
                 torch.cuda.synchronize()
             dist.barrier()
         dist.barrier()

@@ -1,5 +1,8 @@
 """Parity at the full sizes of the benchmark configurations (one GPU's share).
 
+* Headline (the configuration bench.py times): N = 1M, D = 1024, Q = 100,
+  K = 10; all 100 queries checked, 4 of them against the sequential C
+  restatement as well.
 * Config 5 (latency / top-K stress): N = 1M, D = 1024 unit-norm mixture
   (10,000 centres), Q in {1, 16}, K in {10, 256}; every query is checked
   against the oracle.
@@ -39,19 +42,67 @@ def _mixture(oracle_mod, n, nq, dim=1024, centres=10_000):
     return base, queries
 
 
-def test_config5_latency_sweep(engine, oracle_mod, torch_cuda):
-    base, queries = _mixture(oracle_mod, 1_000_000, 16)
-    b16, q16 = oracle_mod.round_fp16(base), oracle_mod.round_fp16(queries)
+@pytest.fixture(scope="module")
+def headline_index(engine, oracle_mod, torch_cuda):
+    """The headline dataset (N = 1M, D = 1024, BASELINE mixture, seeds
+    11/12/13) built once for the tests at that size: (index, fp16-rounded
+    rows, centres)."""
+    c = oracle_mod.gen_centres(10_000, 1024)
+    base = oracle_mod.gen_mixture(1_000_000, 1024, 10_000, oracle_mod.SEED_BASE, centres=c,
+                                  threads=16)
+    idx = engine.Index(0)
+    idx.build(base)
+    b16 = oracle_mod.round_fp16(base)
+    del base
+    yield idx, b16, c
+    idx.close()
+
+
+def _queries(oracle_mod, c, nq):
+    return oracle_mod.gen_mixture(nq, 1024, 10_000, oracle_mod.SEED_QUERIES, centres=c)
+
+
+def test_headline_all_queries(engine, oracle_mod, headline_index):
+    """The configuration bench.py times: N = 1M, D = 1024, Q = 100, K = 10.
+    All 100 queries against the BLAS-seeded oracle (every distance
+    re-checked in float64), and 4 of them against the sequential C
+    restatement of the reference's search on all rows, which needs no seed.
+    Then the same through the device-buffer path, replayed from its graph."""
+    import torch
+
+    idx, b16, c = headline_index
+    queries = _queries(oracle_mod, c, 100)
+    q16 = oracle_mod.round_fp16(queries)
+    i, d = idx.search(queries, 10)
+    oi, od = oracle_mod.blas_knn(b16, q16, 10)
+    par = oracle_mod.check_parity(b16, q16, i, d, oi, od, REL_TOL)
+    assert par.ok, par.detail
+    pick = np.array([0, 33, 66, 99])
+    pi, pd = oracle_mod.port_knn(b16, q16[pick], 10, threads=4)
+    par4 = oracle_mod.check_parity(b16, q16[pick], i[pick], d[pick], pi, pd, REL_TOL)
+    assert par4.ok, par4.detail
+    qd = torch.from_numpy(queries).cuda()
+    ni = torch.empty((100, 10), dtype=torch.int32, device="cuda")
+    nd = torch.empty((100, 10), dtype=torch.float32, device="cuda")
+    for _ in range(4):  # direct, captured, replayed, replayed
+        ni.zero_()
+        idx.search_async(qd, 10, ni, nd)
+        idx.sync()
+        assert np.array_equal(ni.cpu().numpy().view(np.uint32), i)
+        assert np.array_equal(nd.cpu().numpy(), d)
+
+
+def test_config5_latency_sweep(engine, oracle_mod, headline_index):
+    idx, b16, c = headline_index
+    queries = _queries(oracle_mod, c, 16)
+    q16 = oracle_mod.round_fp16(queries)
     oi256, od256 = oracle_mod.blas_knn(b16, q16, 256)
-    with engine.Index(0) as idx:
-        idx.build(base)
-        del base
-        for nq in (1, 16):
-            for k in (10, 256):
-                i, d = idx.search(queries[:nq], k)
-                par = oracle_mod.check_parity(b16, q16[:nq], i, d, oi256[:nq, :k],
-                                              od256[:nq, :k], REL_TOL)
-                assert par.ok, f"Q={nq} K={k}: {par.detail}"
+    for nq in (1, 16):
+        for k in (10, 256):
+            i, d = idx.search(queries[:nq], k)
+            par = oracle_mod.check_parity(b16, q16[:nq], i, d, oi256[:nq, :k],
+                                          od256[:nq, :k], REL_TOL)
+            assert par.ok, f"Q={nq} K={k}: {par.detail}"
 
 
 def test_config4_shard_compute_bound(engine, oracle_mod, torch_cuda):
