@@ -226,7 +226,8 @@ struct knn_index {
   int metric = KNN_METRIC_L2_EXPANDED;
   __half* data = nullptr;
   float* norms = nullptr;
-  CUtensorMap xmap;
+  CUtensorMap xmap;       // 256-row boxes (full tiles)
+  CUtensorMap xmap_tail;  // 32-row boxes (a work unit's narrower last tile)
 
   // exact fp32 re-ranking (knn_index_set_rerank): the fp32 rows are kept
   // by a build made while re-ranking is enabled
@@ -559,7 +560,7 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
   p.err = h->err_dev;
   p.n_rows = h->n;
   p.n_queries = nq;
-  p.row_tiles = plan.row_tiles;
+  p.n_gran = (h->n + knn::kGranRows - 1) / knn::kGranRows;
   p.k = static_cast<int32_t>(ks);
   p.query_block = static_cast<int32_t>(plan.query_block);
   p.query_tiles = static_cast<int32_t>(plan.query_tiles);
@@ -584,7 +585,7 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
     // distance, and the main pass filters with that bound from its first tile
     p.pilot = 1;
     p.pilot_out = h->pilot.as<float>();
-    KNN_CUDA(knn::launch_scan(qmap, h->xmap, p, plan, h->stream, overlap));
+    KNN_CUDA(knn::launch_scan(qmap, h->xmap, h->xmap_tail, p, plan, h->stream, overlap));
     KNN_CUDA(knn::launch_pilot_threshold(p.pilot_out, static_cast<int>(plan.splits),
                                          static_cast<int>(ks), nq, h->thr.as<float>(),
                                          h->stream));
@@ -594,7 +595,7 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
     launches += 2;
   }
   p.bound = h->bound.as<uint32_t>();
-  KNN_CUDA(knn::launch_scan(qmap, h->xmap, p, plan, h->stream, overlap));
+  KNN_CUDA(knn::launch_scan(qmap, h->xmap, h->xmap_tail, p, plan, h->stream, overlap));
   if (prof) KNN_CUDA(cudaEventRecord((*prof)[1], h->stream));
 
   // the lists the final stage merges: the scan's per-unit lists, or one
@@ -970,6 +971,7 @@ int build_impl(knn_index* h, const void* rows, int dtype, int64_t n, int64_t dim
   }
   KNN_CUDA(cudaStreamSynchronize(h->stream));
   int st = encode_rows(&h->xmap, h->data, n, ld, knn::kTileRows);
+  if (st == KNN_OK) st = encode_rows(&h->xmap_tail, h->data, n, ld, knn::kTailBox);
   if (st != KNN_OK) return st;
   ++h->generation;
   drop_graphs(h);
@@ -1139,6 +1141,7 @@ int build_file_impl(knn_index* h, const char* path, int format, int metric, int 
     st = fail(KNN_ECUDA, "dataset upload: %s", cudaGetErrorString(cudaGetLastError()));
   cleanup();
   if (st == KNN_OK) st = encode_rows(&h->xmap, h->data, n, ld, knn::kTileRows);
+  if (st == KNN_OK) st = encode_rows(&h->xmap_tail, h->data, n, ld, knn::kTailBox);
   if (st != KNN_OK) {
     cudaFree(h->data);
     cudaFree(h->norms);
@@ -1643,7 +1646,7 @@ int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
   p.err = h->err_dev;
   p.n_rows = h->n;
   p.n_queries = nq;
-  p.row_tiles = plan.row_tiles;
+  p.n_gran = (h->n + knn::kGranRows - 1) / knn::kGranRows;
   p.k = static_cast<int32_t>(k);
   p.query_block = static_cast<int32_t>(plan.query_block);
   p.query_tiles = static_cast<int32_t>(plan.query_tiles);
@@ -1657,7 +1660,7 @@ int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
   p.pilot_out = nullptr;
   p.thr_init = nullptr;
   p.bound = nullptr;
-  KNN_CUDA(knn::launch_scan(qmap, h->xmap, p, plan, h->stream));
+  KNN_CUDA(knn::launch_scan(qmap, h->xmap, h->xmap_tail, p, plan, h->stream));
   KNN_CUDA(knn::launch_merge(part_d, part_i, k, plan.splits * k, static_cast<int>(plan.splits),
                              static_cast<int>(k), nq, h->row_offset, out_d, out_i, false,
                              h->stream, true, nullptr,

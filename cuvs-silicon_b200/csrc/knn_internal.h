@@ -11,7 +11,9 @@
 namespace knn {
 
 // Scan-kernel geometry (fixed for sm_100a).
-constexpr int kTileRows = 256;    // dataset rows per tile = UMMA N
+constexpr int kTileRows = 256;    // dataset rows per full tile = UMMA N
+constexpr int kGranRows = 32;     // work units split the rows in granules of this many
+constexpr int kTailBox = 32;      // TMA box rows for a unit's last (narrower) tile
 constexpr int kQueryRows = 128;   // query rows per tile  = UMMA M
 constexpr int kKChunk = 64;       // fp16 per 128-byte swizzled row segment
 constexpr int kStageA = kQueryRows * kKChunk * 2;  // 16 KiB query slab
@@ -35,7 +37,7 @@ struct ScanParams {
   int* err;                  // device error word (0 = ok)
   int64_t n_rows;
   int64_t n_queries;
-  int64_t row_tiles;
+  int64_t n_gran;  // ceil(n_rows / kGranRows)
   int32_t k;
   int32_t query_block;  // query rows owned per work unit (multiple of 32, <= 128)
   int32_t query_tiles;
@@ -78,10 +80,12 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
 // Launchers (return the CUDA error of the launch).
 // `overlap` launches the kernel as a programmatic dependent of the one
 // before it (its set-up overlaps that kernel's tail); off when the caller
-// brackets kernels with timing events.
+// brackets kernels with timing events.  xmap: the dataset rows with
+// kTileRows-row boxes; xmap_tail: the same rows with kTailBox-row boxes (a
+// unit's last tile is loaded as several of these).
 cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
-                        const ScanParams& p, const Plan& plan, cudaStream_t stream,
-                        bool overlap = true);
+                        const CUtensorMap& xmap_tail, const ScanParams& p, const Plan& plan,
+                        cudaStream_t stream, bool overlap = true);
 
 // fp32/fp16 rows -> fp16 rows with leading dimension ld (zero padded) plus
 // fp32 norms of the rounded rows.  in_is_half selects the input type.

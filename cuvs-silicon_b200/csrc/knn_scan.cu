@@ -22,10 +22,13 @@
 //                       and merged into the query's shared-memory max-heap
 //                       by warp-uniform flushes (see epilogue()).
 //
-// Work is split into units (query tile m, contiguous range s of dataset
-// tiles).  A persistent CTA walks units blockIdx.x, +gridDim.x, ...; at the
-// end of a unit each query's heap is sorted and written as list s of that
-// query: part[(q * splits + s) * k + r].  The merge kernel (knn_merge.cu)
+// Work is split into units (query tile m, contiguous row range s).  Row
+// ranges are cut in 32-row granules, so every unit of a query tile holds the
+// same number of rows to within one granule: a unit is a run of full
+// 256-row tiles and one narrower last tile (its MMAs use N = its width and
+// its rows arrive as 32-row TMA boxes).  A persistent CTA walks units
+// blockIdx.x, +gridDim.x, ...; at the end of a unit each query's heap is
+// sorted and written as list s of that query: part[(q * splits + s) * k + r].  The merge kernel (knn_merge.cu)
 // reduces the lists to the final top-k, ordered by (distance, index) like
 // src/cagra.cpp:229-238.
 //
@@ -143,13 +146,27 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, const ScanParams& p) {
   return s;
 }
 
-__device__ __forceinline__ void unit_range(const ScanParams& p, int u, int& m, int64_t& t0,
-                                           int64_t& t1) {
-  m = u % p.query_tiles;
-  const int s = u / p.query_tiles;
-  t0 = static_cast<int64_t>(s) * p.row_tiles / p.splits;
-  t1 = static_cast<int64_t>(s + 1) * p.row_tiles / p.splits;
-  if (p.pilot && t1 > t0 + 1) t1 = t0 + 1;  // the pilot pass reads one tile per unit
+// Unit u: query tile m and rows [r0, r_end), whole granules.  At the end of
+// the dataset r_end may pass n_rows by less than a granule: TMA fills those
+// rows with zeros and the epilogue masks them (row norm +inf).  The pilot
+// pass keeps only the unit's first tile.
+struct Unit {
+  int m;
+  int64_t r0, r_end;
+};
+__device__ __forceinline__ Unit unit_of(const ScanParams& p, int u) {
+  Unit x;
+  x.m = u % p.query_tiles;
+  const int64_t s = u / p.query_tiles;
+  x.r0 = s * p.n_gran / p.splits * kGranRows;
+  x.r_end = (s + 1) * p.n_gran / p.splits * kGranRows;
+  if (p.pilot && x.r_end > x.r0 + kTileRows) x.r_end = x.r0 + kTileRows;
+  return x;
+}
+// Width (rows, a multiple of kGranRows) of the tile starting at row rs.
+__device__ __forceinline__ int tile_width(int64_t rs, int64_t r_end) {
+  const int64_t w = r_end - rs;
+  return w < kTileRows ? static_cast<int>(w) : kTileRows;
 }
 
 // Bounded wait used while unwinding after an error: ignores the error word,
@@ -167,23 +184,35 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
 // synchronises before it returns), so the dataset slabs of the first
 // stages are requested before griddepcontrol.wait and only the query slabs
 // wait for it: the first tile's load overlaps the kernels before this one.
-__device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap, const ScanParams& p,
-                         const Smem& sm) {
+// A full tile's slab is one 256-row box; a narrower tile's slab is w / 32
+// boxes of 32 rows placed one after the other, which gives the same
+// shared-memory layout for its first w rows (every box starts on a 1024-byte
+// swizzle atom).
+__device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap,
+                         const CUtensorMap* xmap_tail, const ScanParams& p, const Smem& sm) {
   const uint64_t pol_q = policy_evict_last();
   const uint64_t pol_x = p.dataset_evict_first ? policy_evict_first() : policy_evict_normal();
+  auto load_rows = [&](uint8_t* dst, uint64_t* bar, int kc, int64_t rs, int w) {
+    if (w == kTileRows) {
+      tma_load_2d(dst, xmap, bar, kc * kKChunk, static_cast<int32_t>(rs), pol_x);
+    } else {
+      for (int j = 0; j < w; j += kTailBox)
+        tma_load_2d(dst + j * (kKChunk * 2), xmap_tail, bar, kc * kKChunk,
+                    static_cast<int32_t>(rs + j), pol_x);
+    }
+  };
   // phase 1: dataset slabs of the first p.stages loads (every stage is free)
   uint32_t pre = 0;
   for (int u = blockIdx.x; u < p.units && pre < static_cast<uint32_t>(p.stages);
        u += gridDim.x) {
-    int m;
-    int64_t t0, t1;
-    unit_range(p, u, m, t0, t1);
-    for (int64_t t = t0; t < t1 && pre < static_cast<uint32_t>(p.stages); ++t) {
-      const int32_t xy = static_cast<int32_t>(t * kTileRows);
+    const Unit un = unit_of(p, u);
+    for (int64_t rs = un.r0; rs < un.r_end && pre < static_cast<uint32_t>(p.stages);
+         rs += kTileRows) {
+      const int w = tile_width(rs, un.r_end);
       for (int kc = 0; kc < p.k_chunks && pre < static_cast<uint32_t>(p.stages); ++kc) {
         uint8_t* st = sm.stages + static_cast<size_t>(pre) * kStageBytes;
-        mbar_arrive_expect_tx(&sm.full[pre], kStageBytes);
-        tma_load_2d(st + kStageA, xmap, &sm.full[pre], kc * kKChunk, xy, pol_x);
+        mbar_arrive_expect_tx(&sm.full[pre], kStageA + w * (kKChunk * 2));
+        load_rows(st + kStageA, &sm.full[pre], kc, rs, w);
         ++pre;
       }
     }
@@ -193,12 +222,10 @@ __device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap, const
   uint32_t it = 0;
   bool failed = false;
   for (int u = blockIdx.x; u < p.units && !failed; u += gridDim.x) {
-    int m;
-    int64_t t0, t1;
-    unit_range(p, u, m, t0, t1);
-    const int32_t qy = m * p.query_block;
-    for (int64_t t = t0; t < t1 && !failed; ++t) {
-      const int32_t xy = static_cast<int32_t>(t * kTileRows);
+    const Unit un = unit_of(p, u);
+    const int32_t qy = un.m * p.query_block;
+    for (int64_t rs = un.r0; rs < un.r_end && !failed; rs += kTileRows) {
+      const int w = tile_width(rs, un.r_end);
       for (int kc = 0; kc < p.k_chunks; ++kc) {
         const uint32_t slot = it % p.stages;
         uint8_t* st = sm.stages + static_cast<size_t>(slot) * kStageBytes;
@@ -212,9 +239,9 @@ __device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap, const
           failed = true;
           break;
         }
-        mbar_arrive_expect_tx(&sm.full[slot], kStageBytes);
+        mbar_arrive_expect_tx(&sm.full[slot], kStageA + w * (kKChunk * 2));
         tma_load_2d(st, qmap, &sm.full[slot], kc * kKChunk, qy, pol_q);
-        tma_load_2d(st + kStageA, xmap, &sm.full[slot], kc * kKChunk, xy, pol_x);
+        load_rows(st + kStageA, &sm.full[slot], kc, rs, w);
         ++it;
       }
     }
@@ -228,14 +255,14 @@ __device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap, const
 }
 
 __device__ void mma_issuer(const ScanParams& p, const Smem& sm, uint32_t tmem_base) {
-  constexpr uint32_t idesc = idesc_f16_f32(kQueryRows, kTileRows);
   uint32_t it = 0, tc = 0;
   bool failed = false;
   for (int u = blockIdx.x; u < p.units && !failed; u += gridDim.x) {
-    int m;
-    int64_t t0, t1;
-    unit_range(p, u, m, t0, t1);
-    for (int64_t t = t0; t < t1 && !failed; ++t) {
+    const Unit un = unit_of(p, u);
+    for (int64_t rs = un.r0; rs < un.r_end && !failed; rs += kTileRows) {
+      // N = the tile's width: a narrower last tile multiplies only its rows
+      const uint32_t idesc =
+          idesc_f16_f32(kQueryRows, static_cast<uint32_t>(tile_width(rs, un.r_end)));
       const uint32_t b = tc & 1u;
       if (!mbar_wait(&sm.acc_empty[b], ((tc >> 1) & 1u) ^ 1u, p.err, kErrTimeoutAccEmpty)) {
         failed = true;
@@ -331,33 +358,67 @@ __device__ __forceinline__ void bitonic_sort(float (&g)[32]) {
 
 __device__ __forceinline__ void sort32(float (&g)[32]) { bitonic_sort<2>(g); }
 
-// Per query row (one epilogue lane): the filter threshold, the heap root
-// and the number of buffered survivors.
+// k up to which each query row keeps its running top-k in registers (a
+// sorted array of kRegK keys) instead of a shared-memory heap.
+constexpr int kRegK = 16;
+
+// Per query row (one epilogue lane): the filter threshold, the worst kept
+// key (root), the number of buffered survivors and the top-k itself.
+// kReg: top[] holds kRegK keys in ascending order, the first kRegK - k of
+// them the sentinel 0 (below every real key, so they never leave the front)
+// and the rest the row's k best keys, padded with the empty key; inserting a
+// key drops the largest, so top[kRegK - 1] is the k-th best.  Otherwise the
+// top-k lives in the shared-memory max-heap of the row.
+template <bool kReg>
 struct RowState {
   float thr;     // candidates with d < thr are kept
-  uint64_t root; // heap root key (worst kept entry) once the heap holds k, else empty
+  uint64_t root; // worst kept key once the row holds k, else the empty key
   int cnt;       // survivors waiting in the row's buffer
-  int size;      // entries in the heap (<= k)
+  int size;      // entries in the heap (<= k; heap path only)
   uint32_t pub;  // bound this row last published (order bits)
+  uint64_t top[kReg ? kRegK : 1];
 };
 
-// Moves every lane's buffered survivors into its heap.  Warp-uniform: all
+// Inserts key x into the ascending register array a, dropping its largest
+// key (x >= a[kRegK - 1] leaves it unchanged).  Branch-free: c[i] = x < a[i]
+// for the original keys, then a[i] takes a[i - 1] (shifted up), x, or keeps
+// its key.
+__device__ __forceinline__ void topk_insert(uint64_t (&a)[kRegK], uint64_t x) {
+  bool c[kRegK];
+#pragma unroll
+  for (int i = 0; i < kRegK; ++i) c[i] = x < a[i];
+#pragma unroll
+  for (int i = kRegK - 1; i > 0; --i) a[i] = c[i - 1] ? a[i - 1] : (c[i] ? x : a[i]);
+  a[0] = c[0] ? x : a[0];
+}
+
+// Moves every lane's buffered survivors into its top-k.  Warp-uniform: all
 // lanes run the same number of iterations (the warp's largest buffer), so
-// the heap updates of the 32 query rows proceed in lock-step.  The heap
-// grows by sift-up until it holds k entries, then replaces its root.
-template <int kMetric>
-__device__ __forceinline__ void flush_buffer(RowState& st, const Smem& sm, int k, int stride,
-                                             int row) {
+// the updates of the 32 query rows proceed in lock-step.  Heap path: the
+// heap grows by sift-up until it holds k entries, then replaces its root.
+template <int kMetric, bool kReg>
+__device__ __forceinline__ void flush_buffer(RowState<kReg>& st, const Smem& sm, int k,
+                                             int stride, int row) {
   const int maxc = __reduce_max_sync(0xffffffffu, st.cnt);
-  for (int b = 0; b < maxc; ++b) {
-    if (b < st.cnt) {
-      const uint64_t key = sm.buf[b * stride + row];
-      if (st.size < k) {
-        heap_sift_up(sm.heap, stride, row, st.size, key);
-        if (++st.size == k) st.root = sm.heap[row];
-      } else if (key < st.root) {
-        heap_sift_down(sm.heap, k, stride, row, 0, key);
-        st.root = sm.heap[row];
+  if constexpr (kReg) {
+    for (int b = 0; b < maxc; ++b) {
+      if (b < st.cnt) {
+        const uint64_t key = sm.buf[b * stride + row];
+        if (key < st.top[kRegK - 1]) topk_insert(st.top, key);
+      }
+    }
+    st.root = st.top[kRegK - 1];
+  } else {
+    for (int b = 0; b < maxc; ++b) {
+      if (b < st.cnt) {
+        const uint64_t key = sm.buf[b * stride + row];
+        if (st.size < k) {
+          heap_sift_up(sm.heap, stride, row, st.size, key);
+          if (++st.size == k) st.root = sm.heap[row];
+        } else if (key < st.root) {
+          heap_sift_down(sm.heap, k, stride, row, 0, key);
+          st.root = sm.heap[row];
+        }
       }
     }
   }
@@ -389,7 +450,7 @@ __device__ __forceinline__ void flush_buffer(RowState& st, const Smem& sm, int k
 // on.  A row of the final top-k lies at d <= R and still passes in its own
 // unit, whose best k then include it; units may end with fewer than k
 // entries (padding), which the merge ignores.
-template <int kMetric>
+template <int kMetric, bool kReg>
 __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base, int warp,
                          int lane) {
   const int quad = warp & 3;              // TMEM lane quadrant this warp may access
@@ -401,37 +462,46 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
   uint32_t tc = 0;
   bool failed = false;
   for (int u = blockIdx.x; u < p.units && !failed; u += gridDim.x) {
-    int m;
-    int64_t t0, t1;
-    unit_range(p, u, m, t0, t1);
-    const int64_t q = static_cast<int64_t>(m) * p.query_block + row;
+    const Unit un = unit_of(p, u);
+    // rows at or past row_lim are masked: the dataset's end, or (in a
+    // narrower last tile) accumulator columns the tile's MMAs did not write
+    const int64_t row_lim = un.r_end < p.n_rows ? un.r_end : p.n_rows;
+    const int64_t q = static_cast<int64_t>(un.m) * p.query_block + row;
     const bool valid_q = warp_active && row < p.query_block && q < p.n_queries;
     const float qn = valid_q ? p.query_norms[q] : 0.0f;
-    RowState st;
+    RowState<kReg> st;
     st.thr = valid_q ? (p.thr_init ? p.thr_init[q] : kInf) : __int_as_float(0xff800000);
     st.root = empty_key<kMetric>();
     st.cnt = 0;
     st.size = 0;
     st.pub = 0xFFFFFFFFu;
+    if constexpr (kReg) {
+#pragma unroll
+      for (int i = 0; i < kRegK; ++i) st.top[i] = i < kRegK - k ? 0ull : empty_key<kMetric>();
+    }
     // Row norms are prefetched one tile ahead into registers, then staged in
     // this warp's slice of shared memory so the chunk loop reads them with
     // a shared-memory load instead of waiting on DRAM once per chunk (for
     // the inner product: 0 for a row, +inf past the last row).
     float* const ns = sm.norm_stage + (warp - 2) * kAccCols;
     float nx[kAccCols / 32];
-    auto prefetch_norms = [&](int64_t tile) {
+    auto prefetch_norms = [&](int64_t rs) {
 #pragma unroll
       for (int c = 0; c < kAccCols / 32; ++c) {
-        const int64_t col = tile * kTileRows + c * 32 + lane;
+        const int64_t col = rs + c * 32 + lane;
         if constexpr (kMetric == KNN_METRIC_INNER_PRODUCT) {
-          nx[c] = col < p.n_rows ? 0.0f : kInf;
+          nx[c] = col < row_lim ? 0.0f : kInf;
         } else {
-          nx[c] = col < p.n_rows ? __ldg(p.row_norms + col) : kInf;
+          nx[c] = col < row_lim ? __ldg(p.row_norms + col) : kInf;
         }
       }
     };
-    if (warp_active) prefetch_norms(t0);
-    for (int64_t t = t0; t < t1; ++t) {
+    if (warp_active) prefetch_norms(un.r0);
+    for (int64_t rs = un.r0; rs < un.r_end; rs += kTileRows) {
+      // 32-column chunks of this tile's accumulator, rounded up to a pair
+      // (the TMEM loads go two chunks at a time; a chunk past the tile's
+      // width holds stale columns, masked by their +inf norms)
+      const int nch = ((tile_width(rs, un.r_end) / 32) + 1) & ~1;
       const uint32_t b = tc & 1u;
       // every lane waits; the warp leaves together if any lane gave up, so
       // the .sync.aligned TMEM loads below always see a converged warp
@@ -447,14 +517,14 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
 #pragma unroll
         for (int c = 0; c < kAccCols / 32; ++c) ns[c * 32 + lane] = nx[c];
         __syncwarp();
-        if (t + 1 < t1) prefetch_norms(t + 1);
+        if (rs + kTileRows < un.r_end) prefetch_norms(rs + kTileRows);
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + b * kAccCols;
-        if (t == t0 && (k <= 32 || p.pilot)) {
+        if (rs == un.r0 && (k <= 32 || p.pilot)) {
           float g[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) g[j] = kInf;
 #pragma unroll 1
-          for (int c = 0; c < kAccCols / 32; ++c) {
+          for (int c = 0; c < nch; ++c) {
             uint32_t r[32];
             tmem_ld_32x32b_x32(tbase + c * 32, r);
             tmem_ld_wait_into(r);
@@ -479,10 +549,11 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
             }
           } else {
             // g is ascending, so g[k - 1] = max of g[0..k-1] (written without a
-            // run-time register index)
+            // run-time register index; g[0] is the neutral filler for j >= k
+            // because every g[j] >= g[0], whatever the sign of the distances)
             float tk = g[0];
 #pragma unroll
-            for (int j = 1; j < 32; ++j) tk = fmaxf(tk, j < k ? g[j] : 0.0f);
+            for (int j = 1; j < 32; ++j) tk = fmaxf(tk, j < k ? g[j] : g[0]);
             // keep d <= tk: the next float up
             if (valid_q && tk < kInf) st.thr = fminf(st.thr, next_up(tk));
           }
@@ -499,7 +570,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
             dv[4 * j4 + 2] = dist_from_dot<kMetric>(r[4 * j4 + 2], qn, v.z);
             dv[4 * j4 + 3] = dist_from_dot<kMetric>(r[4 * j4 + 3], qn, v.w);
           }
-          const uint32_t col0 = static_cast<uint32_t>(t * kTileRows + c * 32);
+          const uint32_t col0 = static_cast<uint32_t>(rs + c * 32);
 #pragma unroll
           for (int h = 0; h < 32; h += kRowBuf) {
             uint32_t mask = 0;
@@ -507,7 +578,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
             for (int j = 0; j < kRowBuf; ++j) mask |= (dv[h + j] < st.thr ? 1u : 0u) << j;
             if (__any_sync(0xffffffffu, mask != 0)) {
               if (__any_sync(0xffffffffu, st.cnt + __popc(mask) > kRowBuf)) {
-                flush_buffer<kMetric>(st, sm, k, stride, row);
+                flush_buffer<kMetric, kReg>(st, sm, k, stride, row);
                 mask = 0;
 #pragma unroll
                 for (int j = 0; j < kRowBuf; ++j) mask |= (dv[h + j] < st.thr ? 1u : 0u) << j;
@@ -534,13 +605,13 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
           tmem_ld_32x32b_x32(tbase, ra);
           tmem_ld_wait_into(ra);
 #pragma unroll 1
-          for (int c = 0; c < kAccCols / 32; c += 2) {
+          for (int c = 0; c < nch; c += 2) {
             tmem_ld_32x32b_x32(tbase + (c + 1) * 32, rb);
             process_chunk(ra, c);
             tmem_ld_wait_into(rb);
-            if (c + 2 < kAccCols / 32) tmem_ld_32x32b_x32(tbase + (c + 2) * 32, ra);
+            if (c + 2 < nch) tmem_ld_32x32b_x32(tbase + (c + 2) * 32, ra);
             process_chunk(rb, c + 1);
-            if (c + 2 < kAccCols / 32) tmem_ld_wait_into(ra);
+            if (c + 2 < nch) tmem_ld_wait_into(ra);
           }
         }
       }
@@ -551,8 +622,8 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
       // survivors enter the heap at every tile end so thr tightens early (the
       // accumulator is already released; this overlaps the next tile's MMAs)
       if (warp_active && __any_sync(0xffffffffu, st.cnt > 0)) {
-        flush_buffer<kMetric>(st, sm, k, stride, row);
-        if (p.bound && valid_q && st.size == k) {
+        flush_buffer<kMetric, kReg>(st, sm, k, stride, row);
+        if (p.bound && valid_q && st.root != empty_key<kMetric>()) {
           const uint32_t bits = dist_order_bits(key_dist<kMetric>(st.root));
           if (bits < st.pub) {
             atomicMin(p.bound + q, bits);
@@ -563,8 +634,20 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
     }
     if (failed) break;
     if (p.pilot) continue;
-    if (warp_active) flush_buffer<kMetric>(st, sm, k, stride, row);
-    if (valid_q) {
+    if (warp_active) flush_buffer<kMetric, kReg>(st, sm, k, stride, row);
+    if (kReg && valid_q) {
+      // the row's k best are top[kRegK - k ..], already ascending
+      const int s = u / p.query_tiles;
+      float* od = p.part_d + (static_cast<size_t>(q) * p.splits + s) * k;
+      uint32_t* oi = p.part_i + (static_cast<size_t>(q) * p.splits + s) * k;
+#pragma unroll
+      for (int i = 0; i < (kReg ? kRegK : 0); ++i) {
+        if (i >= kRegK - k) {
+          od[i - (kRegK - k)] = key_dist<kMetric>(st.top[i]);
+          oi[i - (kRegK - k)] = static_cast<uint32_t>(st.top[i]);
+        }
+      }
+    } else if (valid_q) {
       // heap sort of the st.size entries -> ascending (distance, index);
       // the rest of the list is padding
       const int n = st.size;
@@ -586,10 +669,11 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
   }
 }
 
-template <int kMetric>
+template <int kMetric, bool kReg>
 __global__ void __launch_bounds__(kScanThreads, 1)
     knn_scan_kernel(const __grid_constant__ CUtensorMap qmap,
-                    const __grid_constant__ CUtensorMap xmap, const ScanParams p) {
+                    const __grid_constant__ CUtensorMap xmap,
+                    const __grid_constant__ CUtensorMap xmap_tail, const ScanParams p) {
   extern __shared__ uint8_t smem_raw[];
   const Smem sm = carve(smem_raw, p);
   const int warp = threadIdx.x >> 5;
@@ -610,6 +694,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_map(&qmap);
     tma_prefetch_map(&xmap);
+    tma_prefetch_map(&xmap_tail);
   }
   if (warp == 1) {
     tmem_alloc(sm.tmem_slot, kTmemCols);
@@ -628,11 +713,11 @@ __global__ void __launch_bounds__(kScanThreads, 1)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
-    if (lane == 0) producer(&qmap, &xmap, p, sm);
+    if (lane == 0) producer(&qmap, &xmap, &xmap_tail, p, sm);
   } else if (warp == 1) {
     if (lane == 0) mma_issuer(p, sm, tmem_base);
   } else {
-    epilogue<kMetric>(p, sm, tmem_base, warp, lane);
+    epilogue<kMetric, kReg>(p, sm, tmem_base, warp, lane);
   }
 
   tc_fence_before();
@@ -737,21 +822,24 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
   if (stages < 2) return 6;
   const int64_t query_tiles = (n_queries + qb - 1) / qb;
   const int64_t row_tiles = (n_rows + kTileRows - 1) / kTileRows;
+  const int64_t n_gran = (n_rows + kGranRows - 1) / kGranRows;
   int64_t splits;
   if (query_tiles == 1) {
-    splits = row_tiles < num_sms ? row_tiles : num_sms;
+    splits = n_gran < num_sms ? n_gran : num_sms;
   } else {
-    // Pick the split count minimising waves x (tiles per unit + 1), with the
-    // partial lists capped at 1 GiB.
-    const int64_t max_s = row_tiles < 4 * num_sms ? row_tiles : 4 * num_sms;
+    // Pick the split count minimising waves x (tiles per unit + 1), a unit's
+    // narrower last tile counted by its width, with the partial lists capped
+    // at 1 GiB.
+    const int64_t max_s = n_gran < 4 * num_sms ? n_gran : 4 * num_sms;
     splits = 1;
     double best = -1.0;
     for (int64_t s = 1; s <= max_s; ++s) {
       if (n_queries * s * k * 8 > (int64_t(1) << 30) && s > 1) break;
       const int64_t units = query_tiles * s;
       const int64_t waves = (units + num_sms - 1) / num_sms;
-      const int64_t per_unit = (row_tiles + s - 1) / s;
-      const double cost = static_cast<double>(waves) * static_cast<double>(per_unit + 1);
+      const double per_unit =
+          static_cast<double>((n_gran + s - 1) / s) * kGranRows / kTileRows;
+      const double cost = static_cast<double>(waves) * (per_unit + 1.0);
       if (best < 0 || cost < best) {
         best = cost;
         splits = s;
@@ -759,7 +847,7 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
     }
   }
   const int64_t units = query_tiles * splits;
-  if (units > INT32_MAX || row_tiles * kTileRows > INT32_MAX + int64_t(kTileRows)) return 6;
+  if (units > INT32_MAX || n_gran * kGranRows > INT32_MAX + int64_t(kTileRows)) return 6;
   out->query_block = qb;
   out->query_tiles = query_tiles;
   out->row_tiles = row_tiles;
@@ -773,8 +861,9 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
   return 0;
 }
 
-cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap, const ScanParams& p,
-                        const Plan& plan, cudaStream_t stream, bool overlap) {
+cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
+                        const CUtensorMap& xmap_tail, const ScanParams& p, const Plan& plan,
+                        cudaStream_t stream, bool overlap) {
   // the opt-in shared-memory limit is a per-device function attribute
   static std::atomic<bool> configured[64] = {};  // set once; idempotent
   int dev = 0;
@@ -784,14 +873,15 @@ cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap, const 
     return cudaErrorInvalidValue;
   const bool ip = p.metric == KNN_METRIC_INNER_PRODUCT;
   if (dev < 0 || dev >= 64 || !configured[dev]) {
-    e = cudaFuncSetAttribute(knn_scan_kernel<KNN_METRIC_L2_EXPANDED>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemLimit));
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(knn_scan_kernel<KNN_METRIC_INNER_PRODUCT>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemLimit));
-    if (e != cudaSuccess) return e;
+    const void* fns[] = {reinterpret_cast<const void*>(knn_scan_kernel<KNN_METRIC_L2_EXPANDED, false>),
+                         reinterpret_cast<const void*>(knn_scan_kernel<KNN_METRIC_L2_EXPANDED, true>),
+                         reinterpret_cast<const void*>(knn_scan_kernel<KNN_METRIC_INNER_PRODUCT, false>),
+                         reinterpret_cast<const void*>(knn_scan_kernel<KNN_METRIC_INNER_PRODUCT, true>)};
+    for (const void* fn : fns) {
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kSmemLimit));
+      if (e != cudaSuccess) return e;
+    }
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
@@ -804,8 +894,20 @@ cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap, const 
   attr[0].val.programmaticStreamSerializationAllowed = overlap ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (ip) return cudaLaunchKernelEx(&cfg, knn_scan_kernel<KNN_METRIC_INNER_PRODUCT>, qmap, xmap, p);
-  return cudaLaunchKernelEx(&cfg, knn_scan_kernel<KNN_METRIC_L2_EXPANDED>, qmap, xmap, p);
+  if (p.n_gran != (p.n_rows + kGranRows - 1) / kGranRows || p.splits < 1 ||
+      p.splits > p.n_gran)
+    return cudaErrorInvalidValue;
+  // small k: the register top-k (the pilot pass only runs for k > kRegK)
+  const bool reg = p.k <= kRegK && !p.pilot;
+  if (ip)
+    return reg ? cudaLaunchKernelEx(&cfg, knn_scan_kernel<KNN_METRIC_INNER_PRODUCT, true>, qmap,
+                                    xmap, xmap_tail, p)
+               : cudaLaunchKernelEx(&cfg, knn_scan_kernel<KNN_METRIC_INNER_PRODUCT, false>, qmap,
+                                    xmap, xmap_tail, p);
+  return reg ? cudaLaunchKernelEx(&cfg, knn_scan_kernel<KNN_METRIC_L2_EXPANDED, true>, qmap, xmap,
+                                  xmap_tail, p)
+             : cudaLaunchKernelEx(&cfg, knn_scan_kernel<KNN_METRIC_L2_EXPANDED, false>, qmap, xmap,
+                                  xmap_tail, p);
 }
 
 }  // namespace knn
