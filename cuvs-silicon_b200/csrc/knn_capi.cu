@@ -506,6 +506,8 @@ int check_device_error(knn_index* h) {
                   "code %d): every rank must issue each search within that bound "
                   "(knn_index_set_peer_timeout); attach the communicator again before the "
                   "next search", static_cast<double>(h->peer_wait_ns) * 1e-9, code);
+    if (code == knn::kErrBounds)
+      return fail(KNN_ECUDA, "a device bounds check failed (debug build, device code %d)", code);
     return fail(KNN_ETIMEOUT, "scan kernel gave up on a bounded wait (device code %d)", code);
   }
   return KNN_OK;
@@ -561,6 +563,8 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
   p.n_rows = h->n;
   p.n_queries = nq;
   p.n_gran = (h->n + knn::kGranRows - 1) / knn::kGranRows;
+  p.q_rows = nq_pad;
+  p.ld = h->ld;
   p.k = static_cast<int32_t>(ks);
   p.query_block = static_cast<int32_t>(plan.query_block);
   p.query_tiles = static_cast<int32_t>(plan.query_tiles);
@@ -604,12 +608,15 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
   const uint32_t* li = p.part_i;
   int64_t l_stride = ks, q_stride = plan.splits * ks, off = h->row_offset;
   int n_lists = static_cast<int>(plan.splits);
+  const int64_t part_len = nq * plan.splits * ks;  // entries of the per-unit lists
+  int64_t l_len = part_len;
   if (rerank) {
     float* cd = h->cand_d.as<float>();
     uint32_t* ci = h->cand_i.as<uint32_t>();
     KNN_CUDA(knn::launch_merge(p.part_d, p.part_i, ks, plan.splits * ks,
                                static_cast<int>(plan.splits), static_cast<int>(ks), nq, 0, cd,
-                               ci, false, h->stream, overlap));
+                               ci, false, h->stream, overlap, nullptr, false, h->err_dev,
+                               part_len));
     if (!h->comm) {
       KNN_CUDA(knn::launch_rerank(qsrc, h->rows32, h->dim, cd, ci, static_cast<int>(ks),
                                   static_cast<int>(k), nq, h->metric, h->max_norm2,
@@ -632,10 +639,12 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
     q_stride = k;
     n_lists = 1;
     off = 0;
+    l_len = nq * k;
   }
   if (!h->comm) {
     KNN_CUDA(knn::launch_merge(ld, li, l_stride, q_stride, n_lists, static_cast<int>(k), nq,
-                               off, dst_d, dst_i, out_i64, h->stream, overlap, nullptr, neg));
+                               off, dst_d, dst_i, out_i64, h->stream, overlap, nullptr, neg,
+                               h->err_dev, l_len));
     launches += 1;
   } else if (uses_peer_exchange(h, nq, k)) {
     // peer exchange: the local merge writes every query's list into every
@@ -649,10 +658,12 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
     ex.epoch = h->epoch_dev;
     ex.wait_ns = h->peer_wait_ns;
     ex.err = h->err_dev;
+    ex.in_len = l_len;
     ex.mode = 1;
     KNN_CUDA(knn::launch_merge(ld, li, l_stride, q_stride, n_lists, static_cast<int>(k), nq, off,
                                nullptr, nullptr, false, h->stream, overlap, &ex));
     ex.mode = 2;
+    ex.in_len = static_cast<int64_t>(qk) * h->n_ranks;
     ex.dec_d = h->xdec.as<float>();
     ex.dec_i = reinterpret_cast<uint32_t*>(ex.dec_d + qk * h->n_ranks);
     KNN_CUDA(knn::launch_merge(ex.dec_d, ex.dec_i, k, static_cast<int64_t>(h->n_ranks) * k,
@@ -665,7 +676,8 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
     float* send_d = h->gather_send.as<float>();
     uint32_t* send_i = reinterpret_cast<uint32_t*>(send_d + qk);
     KNN_CUDA(knn::launch_merge(ld, li, l_stride, q_stride, n_lists, static_cast<int>(k), nq, off,
-                               send_d, send_i, false, h->stream, overlap));
+                               send_d, send_i, false, h->stream, overlap, nullptr, false,
+                               h->err_dev, l_len));
     ncclResult_t r = nccl().AllGather(h->gather_send.ptr, h->gather_recv.ptr, list_bytes,
                                       ncclUint8, h->comm, h->stream);
     if (r == ncclInProgress) {
@@ -678,7 +690,8 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
     const uint32_t* ri = reinterpret_cast<const uint32_t*>(rd + qk);
     KNN_CUDA(knn::launch_merge(rd, ri, static_cast<int64_t>(2 * qk), k, h->n_ranks,
                                static_cast<int>(k), nq, 0, dst_d, dst_i, out_i64, h->stream,
-                               overlap, nullptr, neg));
+                               overlap, nullptr, neg, h->err_dev,
+                               static_cast<int64_t>(2 * qk) * h->n_ranks));
     launches += 2;
   }
   if (prof) KNN_CUDA(cudaEventRecord((*prof)[2], h->stream));
@@ -1647,6 +1660,8 @@ int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
   p.n_rows = h->n;
   p.n_queries = nq;
   p.n_gran = (h->n + knn::kGranRows - 1) / knn::kGranRows;
+  p.q_rows = nq_pad;
+  p.ld = h->ld;
   p.k = static_cast<int32_t>(k);
   p.query_block = static_cast<int32_t>(plan.query_block);
   p.query_tiles = static_cast<int32_t>(plan.query_tiles);
@@ -1664,7 +1679,8 @@ int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
   KNN_CUDA(knn::launch_merge(part_d, part_i, k, plan.splits * k, static_cast<int>(plan.splits),
                              static_cast<int>(k), nq, h->row_offset, out_d, out_i, false,
                              h->stream, true, nullptr,
-                             h->metric == KNN_METRIC_INNER_PRODUCT));
+                             h->metric == KNN_METRIC_INNER_PRODUCT, h->err_dev,
+                             nq * plan.splits * k));
   if (cd == 0)
     KNN_CUDA(cudaMemcpyAsync(distances, out_d, qk * 4, cudaMemcpyDeviceToHost, h->stream));
   if (cn == 0)

@@ -29,6 +29,14 @@ constexpr int kMaxK = 256;
 constexpr int kRowBuf = 16;       // buffered survivors per query row
 constexpr uint32_t kNoIndex = 0xFFFFFFFFu;
 
+// Device-side error codes (written to a kernel's error word; 0 = ok).
+constexpr int kErrTimeoutFull = 1;      // MMA waiting for a TMA stage
+constexpr int kErrTimeoutEmpty = 2;     // producer waiting for a free stage
+constexpr int kErrTimeoutAccFull = 3;   // epilogue waiting for an accumulator
+constexpr int kErrTimeoutAccEmpty = 4;  // MMA waiting for the epilogue
+constexpr int kErrTimeoutDrain = 5;     // unwinding waits
+constexpr int kErrBounds = 6;           // debug build: a bounds check tripped
+
 struct ScanParams {
   const float* row_norms;    // [n_rows]
   const float* query_norms;  // [n_queries]
@@ -38,6 +46,8 @@ struct ScanParams {
   int64_t n_rows;
   int64_t n_queries;
   int64_t n_gran;  // ceil(n_rows / kGranRows)
+  int64_t q_rows;  // rows of the fp16 query buffer (padded_query_rows)
+  int64_t ld;      // leading dimension of the fp16 rows and queries (halves)
   int32_t k;
   int32_t query_block;  // query rows owned per work unit (multiple of 32, <= 128)
   int32_t query_tiles;
@@ -134,9 +144,10 @@ struct Exchange {
   int mode;               // 0 none; 1 push this rank's lists to every rank; 2 receive and merge
   const uint32_t* epoch;  // device word: the current search's epoch (>= 1)
   uint64_t wait_ns;       // mode 2: how long to wait for a peer's list
-  int* err;               // device error word (wait timeouts)
+  int* err;               // device error word (wait timeouts, debug bounds checks)
   float* dec_d;           // mode 2: received lists, decoded: [q][n_ranks][k]
   uint32_t* dec_i;
+  int64_t in_len;         // entries of the merge's in_d / in_i (debug bounds checks)
 };
 constexpr int kErrTimeoutPeer = 7;  // a peer's list never arrived
 constexpr uint64_t kPeerWaitDefaultNs = 1000000000ull;  // 1 s
@@ -157,11 +168,15 @@ inline int64_t exchange_words(int n_ranks, int64_t cap_qk) {
 // `negate_out` writes -d to out_d (the inner-product metric orders by -q.x
 // internally and reports q.x; padding becomes -inf).  Lists written to an
 // exchange buffer (mode 1) are never negated.
+// err, in_len (optional): the device error word and the number of entries
+// of in_d / in_i, for the debug build's bounds checks (with an exchange,
+// ex->err and ex->in_len are used instead).
 cudaError_t launch_merge(const float* in_d, const uint32_t* in_i, int64_t stride_list,
                          int64_t stride_query, int n_lists, int k, int64_t n_queries,
                          int64_t index_offset, float* out_d, void* out_i, bool out_i64,
                          cudaStream_t stream, bool overlap = true,
-                         const Exchange* ex = nullptr, bool negate_out = false);
+                         const Exchange* ex = nullptr, bool negate_out = false,
+                         int* err = nullptr, int64_t in_len = 0);
 
 // Exact fp32 re-ranking (knn_rerank.cu).  cand_{d,i}: per query the scan's
 // top kc (kc >= k, kc <= kMaxK) sorted candidates, local row indices,

@@ -32,6 +32,7 @@
 #include <cstdint>
 
 #include "knn_internal.h"
+#include "ptx.cuh"
 
 namespace knn {
 
@@ -546,6 +547,12 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
   // that opened this search incremented.  Mode 2 waits for the local merge
   // (mode 1) of this rank too, whose stores carry this rank's own list.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // debug builds: every list this block reads (and, with an exchange, every
+  // slot it writes or polls) lies inside its buffer
+  const int64_t last_in = q * stride_query + static_cast<int64_t>(n_lists - 1) * stride_list + k;
+  if (!in_bounds(ex.in_len <= 0 || last_in <= ex.in_len, ex.err)) return;
+  if (ex.mode != 0 && !in_bounds((q + 1) * k <= ex.cap_qk && ex.n_ranks <= kMaxRanks, ex.err))
+    return;
   const uint32_t epoch = ex.mode != 0 ? *reinterpret_cast<const volatile uint32_t*>(ex.epoch) : 0u;
   if (ex.mode == 2) {
     if (receive_lists(ex, epoch, q, k, &s_abort))
@@ -614,10 +621,12 @@ cudaError_t launch_merge(const float* in_d, const uint32_t* in_i, int64_t stride
                          int64_t stride_query, int n_lists, int k, int64_t n_queries,
                          int64_t index_offset, float* out_d, void* out_i, bool out_i64,
                          cudaStream_t stream, bool overlap, const Exchange* ex_opt,
-                         bool negate_out) {
+                         bool negate_out, int* err, int64_t in_len) {
   if (n_queries <= 0 || k <= 0) return cudaSuccess;
   const float sign = negate_out ? -1.0f : 1.0f;
   Exchange none = {};
+  none.err = err;
+  none.in_len = in_len;
   const Exchange& ex = ex_opt ? *ex_opt : none;
   if (n_queries > 0x7fffffff) return cudaErrorInvalidValue;
   if (k <= 32)

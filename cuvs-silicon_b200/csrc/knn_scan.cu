@@ -60,13 +60,15 @@ namespace {
 template <int kMetric>
 __device__ __forceinline__ uint64_t make_key(float d, uint32_t i) {
   uint32_t u = __float_as_uint(d);
-  if constexpr (kMetric == KNN_METRIC_INNER_PRODUCT) u ^= (u >> 31) ? 0xFFFFFFFFu : 0x80000000u;
+  if constexpr (kMetric == KNN_METRIC_INNER_PRODUCT)
+    u ^= static_cast<uint32_t>(static_cast<int32_t>(u) >> 31) | 0x80000000u;  // branch-free
   return (static_cast<uint64_t>(u) << 32) | i;
 }
 template <int kMetric>
 __device__ __forceinline__ float key_dist(uint64_t key) {
   uint32_t b = static_cast<uint32_t>(key >> 32);
-  if constexpr (kMetric == KNN_METRIC_INNER_PRODUCT) b ^= (b >> 31) ? 0x80000000u : 0xFFFFFFFFu;
+  if constexpr (kMetric == KNN_METRIC_INNER_PRODUCT)
+    b ^= ~static_cast<uint32_t>(static_cast<int32_t>(b) >> 31) | 0x80000000u;
   return __uint_as_float(b);
 }
 // (+inf, no index)
@@ -81,7 +83,8 @@ __host__ __device__ constexpr uint64_t empty_key() {
 // at [pos * stride + row], so the 32 threads of a warp always touch 32
 // consecutive 8-byte words whatever positions they visit.
 __device__ __forceinline__ void heap_sift_down(uint64_t* h, int size, int stride, int row, int pos,
-                                               uint64_t key) {
+                                               uint64_t key, int cap, int* err) {
+  if (!in_bounds(size <= cap && pos < cap && row < stride, err)) return;
   while (true) {
     int c = 2 * pos + 1;
     if (c >= size) break;
@@ -102,7 +105,8 @@ __device__ __forceinline__ void heap_sift_down(uint64_t* h, int size, int stride
 
 // Adds `key` at position pos (= the heap's current size) of a max-heap.
 __device__ __forceinline__ void heap_sift_up(uint64_t* h, int stride, int row, int pos,
-                                             uint64_t key) {
+                                             uint64_t key, int cap, int* err) {
+  if (!in_bounds(pos < cap && row < stride, err)) return;
   while (pos > 0) {
     const int parent = (pos - 1) >> 1;
     const uint64_t pk = h[parent * stride + row];
@@ -193,6 +197,11 @@ __device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap,
   const uint64_t pol_q = policy_evict_last();
   const uint64_t pol_x = p.dataset_evict_first ? policy_evict_first() : policy_evict_normal();
   auto load_rows = [&](uint8_t* dst, uint64_t* bar, int kc, int64_t rs, int w) {
+    // rows past n_rows (less than a granule) are TMA's zero fill
+    if (!in_bounds(rs >= 0 && rs < p.n_rows && w > 0 && w <= kTileRows && w % kTailBox == 0 &&
+                       kc * kKChunk < p.ld,
+                   p.err))
+      return;
     if (w == kTileRows) {
       tma_load_2d(dst, xmap, bar, kc * kKChunk, static_cast<int32_t>(rs), pol_x);
     } else {
@@ -224,6 +233,10 @@ __device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap,
   for (int u = blockIdx.x; u < p.units && !failed; u += gridDim.x) {
     const Unit un = unit_of(p, u);
     const int32_t qy = un.m * p.query_block;
+    if (!in_bounds(qy >= 0 && qy + kQueryRows <= p.q_rows, p.err)) {
+      failed = true;
+      break;
+    }
     for (int64_t rs = un.r0; rs < un.r_end && !failed; rs += kTileRows) {
       const int w = tile_width(rs, un.r_end);
       for (int kc = 0; kc < p.k_chunks; ++kc) {
@@ -398,8 +411,9 @@ __device__ __forceinline__ void topk_insert(uint64_t (&a)[kRegK], uint64_t x) {
 // heap grows by sift-up until it holds k entries, then replaces its root.
 template <int kMetric, bool kReg>
 __device__ __forceinline__ void flush_buffer(RowState<kReg>& st, const Smem& sm, int k,
-                                             int stride, int row) {
+                                             int stride, int row, int* err) {
   const int maxc = __reduce_max_sync(0xffffffffu, st.cnt);
+  if (!in_bounds(maxc <= kRowBuf, err)) return;
   if constexpr (kReg) {
     for (int b = 0; b < maxc; ++b) {
       if (b < st.cnt) {
@@ -413,10 +427,10 @@ __device__ __forceinline__ void flush_buffer(RowState<kReg>& st, const Smem& sm,
       if (b < st.cnt) {
         const uint64_t key = sm.buf[b * stride + row];
         if (st.size < k) {
-          heap_sift_up(sm.heap, stride, row, st.size, key);
+          heap_sift_up(sm.heap, stride, row, st.size, key, k, err);
           if (++st.size == k) st.root = sm.heap[row];
         } else if (key < st.root) {
-          heap_sift_down(sm.heap, k, stride, row, 0, key);
+          heap_sift_down(sm.heap, k, stride, row, 0, key, k, err);
           st.root = sm.heap[row];
         }
       }
@@ -492,7 +506,8 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
         if constexpr (kMetric == KNN_METRIC_INNER_PRODUCT) {
           nx[c] = col < row_lim ? 0.0f : kInf;
         } else {
-          nx[c] = col < row_lim ? __ldg(p.row_norms + col) : kInf;
+          nx[c] = col < row_lim && in_bounds(col < p.n_rows, p.err) ? __ldg(p.row_norms + col)
+                                                                     : kInf;
         }
       }
     };
@@ -512,7 +527,8 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
       }
       tc_fence_after();
       uint32_t shared_b = 0xFFFFFFFFu;  // read now, applied before the chunk loop
-      if (p.bound && valid_q) shared_b = *reinterpret_cast<volatile const uint32_t*>(p.bound + q);
+      if (p.bound && valid_q && in_bounds(q < p.n_queries, p.err))
+        shared_b = *reinterpret_cast<volatile const uint32_t*>(p.bound + q);
       if (warp_active) {
 #pragma unroll
         for (int c = 0; c < kAccCols / 32; ++c) ns[c * 32 + lane] = nx[c];
@@ -540,7 +556,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
           }
           sort32(g);
           if (p.pilot) {
-            if (valid_q) {
+            if (valid_q && in_bounds(q < p.n_queries && u / p.query_tiles < p.splits, p.err)) {
               float4* o = reinterpret_cast<float4*>(
                   p.pilot_out + (q * p.splits + u / p.query_tiles) * 32);
 #pragma unroll
@@ -578,7 +594,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
             for (int j = 0; j < kRowBuf; ++j) mask |= (dv[h + j] < st.thr ? 1u : 0u) << j;
             if (__any_sync(0xffffffffu, mask != 0)) {
               if (__any_sync(0xffffffffu, st.cnt + __popc(mask) > kRowBuf)) {
-                flush_buffer<kMetric, kReg>(st, sm, k, stride, row);
+                flush_buffer<kMetric, kReg>(st, sm, k, stride, row, p.err);
                 mask = 0;
 #pragma unroll
                 for (int j = 0; j < kRowBuf; ++j) mask |= (dv[h + j] < st.thr ? 1u : 0u) << j;
@@ -586,7 +602,8 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
 #pragma unroll
               for (int j = 0; j < kRowBuf; ++j) {
                 if ((mask >> j) & 1u) {
-                  sm.buf[st.cnt * stride + row] = make_key<kMetric>(dv[h + j], col0 + h + j);
+                  if (in_bounds(st.cnt < kRowBuf, p.err))
+                    sm.buf[st.cnt * stride + row] = make_key<kMetric>(dv[h + j], col0 + h + j);
                   ++st.cnt;
                 }
               }
@@ -622,10 +639,10 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
       // survivors enter the heap at every tile end so thr tightens early (the
       // accumulator is already released; this overlaps the next tile's MMAs)
       if (warp_active && __any_sync(0xffffffffu, st.cnt > 0)) {
-        flush_buffer<kMetric, kReg>(st, sm, k, stride, row);
+        flush_buffer<kMetric, kReg>(st, sm, k, stride, row, p.err);
         if (p.bound && valid_q && st.root != empty_key<kMetric>()) {
           const uint32_t bits = dist_order_bits(key_dist<kMetric>(st.root));
-          if (bits < st.pub) {
+          if (bits < st.pub && in_bounds(q < p.n_queries, p.err)) {
             atomicMin(p.bound + q, bits);
             st.pub = bits;
           }
@@ -634,8 +651,10 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
     }
     if (failed) break;
     if (p.pilot) continue;
-    if (warp_active) flush_buffer<kMetric, kReg>(st, sm, k, stride, row);
-    if (kReg && valid_q) {
+    if (warp_active) flush_buffer<kMetric, kReg>(st, sm, k, stride, row, p.err);
+    const bool out_ok = !valid_q || in_bounds(q < p.n_queries && u / p.query_tiles < p.splits,
+                                              p.err);
+    if (kReg && valid_q && out_ok) {
       // the row's k best are top[kRegK - k ..], already ascending
       const int s = u / p.query_tiles;
       float* od = p.part_d + (static_cast<size_t>(q) * p.splits + s) * k;
@@ -647,7 +666,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
           oi[i - (kRegK - k)] = static_cast<uint32_t>(st.top[i]);
         }
       }
-    } else if (valid_q) {
+    } else if (valid_q && out_ok) {
       // heap sort of the st.size entries -> ascending (distance, index);
       // the rest of the list is padding
       const int n = st.size;
@@ -655,7 +674,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
         const uint64_t top = sm.heap[row];
         const uint64_t last = sm.heap[end * stride + row];
         sm.heap[end * stride + row] = top;
-        heap_sift_down(sm.heap, end, stride, row, 0, last);
+        heap_sift_down(sm.heap, end, stride, row, 0, last, k, p.err);
       }
       const int s = u / p.query_tiles;
       float* od = p.part_d + (static_cast<size_t>(q) * p.splits + s) * k;
@@ -764,7 +783,7 @@ __global__ void __launch_bounds__(256)
   const int r = (k + j - 1) / j;  // <= splits
   extern __shared__ float sv[];   // [splits]
   for (int s = threadIdx.x; s < splits; s += blockDim.x) {
-    const float v = pilot[(q * splits + s) * 32 + (j - 1)];
+    const float v = pilot[(q * splits + s) * 32 + (j - 1)];  // j <= 32
     sv[s] = v == v ? v : kInf;  // NaN counts as +inf
   }
   __syncthreads();

@@ -10,17 +10,35 @@
 #include <cstdint>
 #include <cuda.h>
 
+#include "knn_internal.h"
+
 namespace knn {
 
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s per wait
 
-// Device-side error codes (written to the kernel's error word).
-constexpr int kErrTimeoutFull = 1;      // MMA waiting for a TMA stage
-constexpr int kErrTimeoutEmpty = 2;     // producer waiting for a free stage
-constexpr int kErrTimeoutAccFull = 3;   // epilogue waiting for an accumulator
-constexpr int kErrTimeoutAccEmpty = 4;  // MMA waiting for the epilogue
-constexpr int kErrTimeoutDrain = 5;     // unwinding waits
-constexpr int kErrBounds = 6;           // debug bounds check tripped
+// Device-side error codes: knn_internal.h.
+
+// Debug builds (make DEBUG_BOUNDS=1, lib/libcuvs_b200_debug.so) check the
+// indices the kernels compute before each access they guard: a failed check
+// records kErrBounds in the kernel's error word (the host then reports
+// KNN_ECUDA) and the access is skipped.  Release builds compile the checks
+// away.  This stands in for a memory checker on pools where none can run.
+#ifndef KNN_DEBUG_BOUNDS
+#define KNN_DEBUG_BOUNDS 0
+#endif
+__device__ __forceinline__ bool in_bounds(bool ok, int* err) {
+#if KNN_DEBUG_BOUNDS
+  if (!ok) {
+    if (err) atomicCAS(err, 0, kErrBounds);
+    return false;
+  }
+  return true;
+#else
+  (void)ok;
+  (void)err;
+  return true;
+#endif
+}
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
