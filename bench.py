@@ -31,6 +31,8 @@ Printed on rank 0, one JSON line:
   clocks       SM clock samples (NVML) during the timed region
 
 --impl reference times the reference's CPU implementation alone (rank 0).
+--sweep c5 runs BASELINE config 5 (Q in {1, 16} x K in {10, 256}) on one
+index and prints one line per combination.
 """
 from __future__ import annotations
 
@@ -71,6 +73,9 @@ def parse():
                     help="exact fp32 re-ranking of the fp16 scan's candidates")
     ap.add_argument("--no-graphs", action="store_true",
                     help="launch every search directly instead of replaying CUDA graphs")
+    ap.add_argument("--sweep", default=None, choices=["c5"],
+                    help="c5: BASELINE config 5 (Q in {1, 16} x K in {10, 256}) on one index, "
+                         "one JSON line per combination (the default run prints one line)")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     return a
@@ -295,6 +300,9 @@ def full_dataset_fp16_host(torch, a, centres, dev):
     return out
 
 
+C5_SWEEP = [(1, 10), (1, 256), (16, 10), (16, 256)]  # Q x K
+
+
 def run_engine(a):
     import numpy as np
     import torch
@@ -314,13 +322,17 @@ def run_engine(a):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=dev)
 
+    combos = C5_SWEEP if a.sweep == "c5" else [(a.q, a.k)]
+    max_q = max(q for q, _ in combos)
+    max_k = max(k for _, k in combos)
+
     # ---- data (synthetic, on device)
     cg = torch.Generator(device=dev)
     cg.manual_seed(11)
     centres = torch.randn((a.centres, a.dim), generator=cg, device=dev)
     lo, hi = E.shard_range(a.n, world, rank)
     shard = gen_mixture_device(torch, a.n, lo, hi, a.dim, centres, 12, dev)
-    queries = gen_mixture_device(torch, a.q, 0, a.q, a.dim, centres, 13, dev)
+    all_queries = gen_mixture_device(torch, max_q, 0, max_q, a.dim, centres, 13, dev)
 
     # all engine work and every timing event on one explicit stream (the
     # legacy default stream's handle is 0, which the engine reads as "use
@@ -349,9 +361,6 @@ def run_engine(a):
         dist.broadcast_object_list(obj, src=0)
         idx.attach_comm(obj[0], world, rank)
 
-    out_i = torch.empty((a.q, a.k), dtype=torch.int32, device=dev)
-    out_d = torch.empty((a.q, a.k), dtype=torch.float32, device=dev)
-
     def barrier():
         if world > 1:
             dist.barrier()
@@ -365,136 +374,145 @@ def run_engine(a):
         v = t.cpu().tolist()
         return v if isinstance(x, list) else v[0]
 
-    # ---- warm-up
-    for _ in range(a.warmup):
-        idx.search_async(queries, a.k, out_i, out_d)
-    idx.sync()
+    def measure(nq, k):
+        """Throughput, kernel split, latency and end-to-end QPS of Q = nq, K = k."""
+        queries = all_queries[:nq].contiguous()
+        out_i = torch.empty((nq, k), dtype=torch.int32, device=dev)
+        out_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
+        # ---- warm-up
+        for _ in range(a.warmup):
+            idx.search_async(queries, k, out_i, out_d)
+        idx.sync()
+        r = {}
+        # ---- device-resident timing (value)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        idx.reset_kernel_stats()
+        barrier()
+        ev0.record(stream)
+        for _ in range(a.steps):
+            idx.search_async(queries, k, out_i, out_d)
+        ev1.record(stream)
+        idx.sync()
+        torch.cuda.synchronize()
+        r["dev_ms"] = max_over_ranks(ev0.elapsed_time(ev1))
+        launches = idx.kernel_stats()["kernel_launches"]
+        r["launches_total"] = int(max_over_ranks(float(launches)) * world)
+        r["value"] = nq * a.steps / (r["dev_ms"] / 1000.0)
+        # ---- kernel timing for the roofline (events around the scan kernel)
+        idx.set_profiling(True)
+        idx.reset_kernel_stats()
+        barrier()
+        for _ in range(a.steps):
+            idx.search_async(queries, k, out_i, out_d)
+        idx.sync()
+        st = idx.kernel_stats()
+        idx.set_profiling(False)
+        r["scan_ms"] = max_over_ranks(st["scan_ms"] / max(1, st["scan_launches"]))
+        r["merge_ms"] = max_over_ranks(st["merge_ms"] / max(1, st["scan_launches"]))
+        # ---- device-resident latency: one search at a time, events around each
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(a.steps)]
+        barrier()
+        for e0, e1 in evs:
+            e0.record(stream)
+            idx.search_async(queries, k, out_i, out_d)
+            e1.record(stream)
+            idx.sync()
+        torch.cuda.synchronize()
+        r["lat_dev"] = max_over_ranks([e0.elapsed_time(e1) for e0, e1 in evs])
+        # ---- end-to-end through the public API with pinned host buffers
+        q_host = queries.cpu().pin_memory()
+        i_host = torch.empty((nq, k), dtype=torch.int32).pin_memory()
+        d_host = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+        for _ in range(3):
+            idx.search(q_host, k, neighbors=i_host, distances=d_host)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(a.steps):
+            idx.search(q_host, k, neighbors=i_host, distances=d_host)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        r["e2e"] = nq * a.steps / (max_over_ranks(e0.elapsed_time(e1)) / 1000.0)
+        # per-batch wall-clock latency of the blocking call (the reference's
+        # benchmark times each cagra::search call with a host clock)
+        lat = []
+        barrier()
+        for _ in range(a.steps):
+            t0 = time.perf_counter()
+            idx.search(q_host, k, neighbors=i_host, distances=d_host)
+            lat.append(1000.0 * (time.perf_counter() - t0))
+        r["lat_e2e"] = max_over_ranks(lat)
+        r["nbrs"] = i_host.numpy().view("uint32").copy()
+        r["dists"] = d_host.numpy().copy()
+        # every rank holds the merged global result: do they agree?
+        r["ranks_agree"] = True
+        if world > 1:
+            mine = torch.from_numpy(np.concatenate([r["nbrs"].view(np.int32).ravel(),
+                                                    r["dists"].view(np.int32).ravel()])).to(dev)
+            allr = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(allr, mine)
+            r["ranks_agree"] = all(bool(torch.equal(allr[0], t)) for t in allr)
+        return r
 
     clk = ClockSampler(local)
     clk.__enter__()
-    # ---- device-resident timing (value)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    idx.reset_kernel_stats()
-    barrier()
-    ev0.record(stream)
-    for _ in range(a.steps):
-        idx.search_async(queries, a.k, out_i, out_d)
-    ev1.record(stream)
-    idx.sync()
-    torch.cuda.synchronize()
-    dev_ms = max_over_ranks(ev0.elapsed_time(ev1))
-    launches = idx.kernel_stats()["kernel_launches"]
-    launches_total = int(max_over_ranks(float(launches)) * world)
-    value = a.q * a.steps / (dev_ms / 1000.0)
-
-    # ---- kernel timing for the roofline (events around the scan kernel)
-    idx.set_profiling(True)
-    idx.reset_kernel_stats()
-    barrier()
-    for _ in range(a.steps):
-        idx.search_async(queries, a.k, out_i, out_d)
-    idx.sync()
-    st = idx.kernel_stats()
-    idx.set_profiling(False)
-    scan_ms = max_over_ranks(st["scan_ms"] / max(1, st["scan_launches"]))
-    merge_ms = max_over_ranks(st["merge_ms"] / max(1, st["scan_launches"]))
-
-    # ---- device-resident latency: one search at a time, events around each
-    lat_dev = []
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(a.steps)]
-    barrier()
-    for e0, e1 in evs:
-        e0.record(stream)
-        idx.search_async(queries, a.k, out_i, out_d)
-        e1.record(stream)
-        idx.sync()
-    torch.cuda.synchronize()
-    lat_dev = max_over_ranks([e0.elapsed_time(e1) for e0, e1 in evs])
-
-    # ---- end-to-end through the public API with pinned host buffers
-    q_host = queries.cpu().pin_memory()
-    i_host = torch.empty((a.q, a.k), dtype=torch.int32).pin_memory()
-    d_host = torch.empty((a.q, a.k), dtype=torch.float32).pin_memory()
-    for _ in range(3):
-        idx.search(q_host, a.k, neighbors=i_host, distances=d_host)
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(a.steps):
-        idx.search(q_host, a.k, neighbors=i_host, distances=d_host)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-    e2e = a.q * a.steps / (e2e_ms / 1000.0)
-    # per-batch wall-clock latency of the blocking call (the reference's
-    # benchmark times each cagra::search call with a host clock)
-    lat_e2e = []
-    barrier()
-    for _ in range(a.steps):
-        t0 = time.perf_counter()
-        idx.search(q_host, a.k, neighbors=i_host, distances=d_host)
-        lat_e2e.append(1000.0 * (time.perf_counter() - t0))
-    lat_e2e = max_over_ranks(lat_e2e)
+    results = [measure(q, k) for q, k in combos]
     clk.__exit__(None, None, None)
-    gpu_nbrs = i_host.numpy().view("uint32").copy()
-    gpu_dists = d_host.numpy().copy()
-
-    # every rank holds the merged global result: do they agree?
-    ranks_agree = True
-    if world > 1:
-        mine = torch.from_numpy(np.concatenate([gpu_nbrs.view(np.int32).ravel(),
-                                                gpu_dists.view(np.int32).ravel()])).to(dev)
-        allr = [torch.empty_like(mine) for _ in range(world)]
-        dist.all_gather(allr, mine)
-        ranks_agree = all(bool(torch.equal(allr[0], t)) for t in allr)
 
     # ---- CPU baselines (rank 0, N = 1 only; bounded samples) and parity
-    # (rank 0, every N)
+    # (rank 0, every N): one run of the reference at the largest k, sliced
+    # for the smaller ones (its top-k is a prefix of its top-K)
     cpu = None
     extra = {}
-    parity = None
+    oracle_out = None
     if check:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle
 
         threads = host_threads()
-        q16 = (queries if a.rerank else queries.half().float()).cpu().numpy()
+        q16 = (all_queries if a.rerank else all_queries.half().float()).cpu().numpy()
         if world == 1:
-            sample = max(1, min(a.q, 2 * threads))
-            qps, secs, ref_i, ref_d, kind = cpu_reference_qps(host_base, q16, a.k, sample,
+            sample = max(1, min(max_q, 2 * threads))
+            qps, secs, ref_i, ref_d, kind = cpu_reference_qps(host_base, q16, max_k, sample,
                                                               threads)
-            cpu = {"value": qps, "unit": UNIT, "cores": min(threads, sample), "kind": kind,
-                   "sample": f"{sample} of {a.q} queries against all {a.n} rows "
-                             f"({secs:.1f} s, reference cagra::search, one query slice "
-                             f"per thread)"}
-            try:
-                t0 = time.perf_counter()
-                oracle.blas_knn(host_base, q16, a.k)
-                bt = time.perf_counter() - t0
-                extra["cpu_blas_expanded_form"] = {
-                    "value": a.q / bt, "unit": UNIT, "cores": threads, "kind": "port",
-                    "sample": f"all {a.q} queries, numpy float32 matmul "
-                              f"(OpenBLAS sgemm, {oracle.blas_threads()}), {bt:.1f} s"}
-            except Exception as e:  # informational only
-                extra["cpu_blas_expanded_form"] = {"error": str(e)[:200]}
+            if a.sweep is None:
+                cpu = {"value": qps, "unit": UNIT, "cores": min(threads, sample), "kind": kind,
+                       "sample": f"{sample} of {max_q} queries against all {a.n} rows "
+                                 f"({secs:.1f} s, reference cagra::search, one query slice "
+                                 f"per thread)"}
+                try:
+                    t0 = time.perf_counter()
+                    oracle.blas_knn(host_base, q16, a.k)
+                    bt = time.perf_counter() - t0
+                    extra["cpu_blas_expanded_form"] = {
+                        "value": a.q / bt, "unit": UNIT, "cores": threads, "kind": "port",
+                        "sample": f"all {a.q} queries, numpy float32 matmul "
+                                  f"(OpenBLAS sgemm, {oracle.blas_threads()}), {bt:.1f} s"}
+                except Exception as e:  # informational only
+                    extra["cpu_blas_expanded_form"] = {"error": str(e)[:200]}
         else:
             # the merged multi-rank result against the whole dataset, which
             # no rank holds: regenerate it here
-            t0 = time.perf_counter()
             host_base = full_dataset_fp16_host(torch, a, centres, dev)
-            sample = max(1, min(a.q, 16))
-            _, secs, ref_i, ref_d, kind = cpu_reference_qps(host_base, q16, a.k, sample,
+            sample = max(1, min(max_q, 16))
+            _, secs, ref_i, ref_d, kind = cpu_reference_qps(host_base, q16, max_k, sample,
                                                             threads)
-            secs = time.perf_counter() - t0
-        par = (oracle.check_parity(host_base, q16[:sample], gpu_nbrs[:sample],
-                                   gpu_dists[:sample], ref_i, ref_d, 1e-3)
+        oracle_out = (host_base, q16, sample, ref_i, ref_d, kind, oracle)
+
+    def parity_of(r, nq, k):
+        if oracle_out is None:
+            return None
+        base, q16, sample, ref_i, ref_d, kind, oracle = oracle_out
+        m = min(sample, nq)
+        oi, od = ref_i[:m, :k], ref_d[:m, :k]
+        par = (oracle.check_parity(base, q16[:m], r["nbrs"][:m], r["dists"][:m], oi, od, 1e-3)
                if not a.rerank else None)
-        exact = (bool(np.array_equal(gpu_nbrs[:sample], ref_i)
-                      and np.array_equal(gpu_dists[:sample], ref_d)) if a.rerank else None)
-        parity = {
-            "ok": bool(par.ok if par is not None else exact) and ranks_agree,
-            "queries_checked": sample, "of": a.q,
+        exact = (bool(np.array_equal(r["nbrs"][:m], oi) and np.array_equal(r["dists"][:m], od))
+                 if a.rerank else None)
+        return {
+            "ok": bool(par.ok if par is not None else exact) and r["ranks_agree"],
+            "queries_checked": m, "of": nq,
             "oracle": ("reference cagra::search (oracle/_ref, the reference's "
                        "src/cagra.cpp compiled unmodified)" if kind == "reference"
                        else "C restatement of src/cagra.cpp:211-252 (oracle/knn_oracle.c)"),
@@ -502,57 +520,62 @@ def run_engine(a):
                      "oracle.check_parity on fp16-rounded rows: index equal or float64 "
                      "distances within rel 1e-3; recall@k 1.0; sorted; padding"),
             "detail": par.detail if par is not None else f"identical={exact}",
-            "ranks_agree": ranks_agree,
+            "ranks_agree": r["ranks_agree"],
             "result_of": f"the last end-to-end search, merged over {world} rank(s)",
         }
-        del host_base
 
     n_shard = hi - lo
     peak, peak_kind = peaks()
-    achieved = (n_shard * a.dim * 2) / (scan_ms / 1000.0) / 1e9
-    traffic = profile_traffic(a, n_shard)
     shard_mb = n_shard * a.dim * 2 / 2 ** 20
     if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-            "steps": a.steps, "warmup": a.warmup, "ms_per_step": dev_ms / a.steps,
-            "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": value / PUBLISHED_QPS, "dtype": "f16",
-            "data": "synthetic: unit-norm Gaussian mixture (10,000 centres, sigma 0.3), "
-                    "generated on device with torch (seeds 11/12/13)",
-            "config": {"workload": workload_name(a), "n_rows": a.n, "dim": a.dim,
-                       "n_queries": a.q, "k": a.k,
-                       "metric": "InnerProduct" if a.metric == "ip" else "L2Expanded",
-                       "exact_fp32_rerank": bool(a.rerank),
-                       "parallelism": f"row-shard x{world}" + (
-                           " + NVLink peer exchange of the per-rank top-k lists"
-                           if world > 1 else ""),
-                       "l2": f"inputs larger than L2 (dataset shard {shard_mb:.0f} MiB "
-                             f"> 126 MiB), no flush" if shard_mb > 126 else
-                             f"dataset shard {shard_mb:.0f} MiB fits in the 126 MiB L2 "
-                             f"(no flush): not an HBM measurement"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic,
-                         "peak_kind": peak_kind, "kernel": "knn_scan_kernel",
-                         "kernel_ms": scan_ms, "merge_ms": merge_ms,
-                         "algorithmic_bytes_per_launch": n_shard * a.dim * 2},
-            "cpu_baseline": cpu,
-            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": a.q * a.dim * 4,
-                    "d2h_bytes_per_step": a.q * a.k * 8},
-            "latency": {
-                "e2e_p50_ms": nearest_rank(lat_e2e, 50), "e2e_p99_ms": nearest_rank(lat_e2e, 99),
-                "device_p50_ms": nearest_rank(lat_dev, 50),
-                "device_p99_ms": nearest_rank(lat_dev, 99),
-                "samples": a.steps,
-                "how": "one batch at a time; e2e = host clock around the blocking search "
-                       "with pinned host buffers; device = CUDA events around one "
-                       "device-resident search; max over ranks per sample; nearest rank"},
-            "parity": parity,
-            "gpu_launches": launches_total,
-            "clocks": clk.summary(),
-        }
-        line.update(extra)
-        emit(line)
+        for (nq, k), r in zip(combos, results):
+            aa = argparse.Namespace(**vars(a))
+            aa.q, aa.k = nq, k
+            achieved = (n_shard * a.dim * 2) / (r["scan_ms"] / 1000.0) / 1e9
+            line = {
+                "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": world,
+                "steps": a.steps, "warmup": a.warmup, "ms_per_step": r["dev_ms"] / a.steps,
+                "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": r["value"] / PUBLISHED_QPS, "dtype": "f16",
+                "data": "synthetic: unit-norm Gaussian mixture (10,000 centres, sigma 0.3), "
+                        "generated on device with torch (seeds 11/12/13)",
+                "config": {"workload": workload_name(aa), "n_rows": a.n, "dim": a.dim,
+                           "n_queries": nq, "k": k,
+                           "metric": "InnerProduct" if a.metric == "ip" else "L2Expanded",
+                           "exact_fp32_rerank": bool(a.rerank),
+                           "parallelism": f"row-shard x{world}" + (
+                               " + NVLink peer exchange of the per-rank top-k lists"
+                               if world > 1 else ""),
+                           "l2": f"inputs larger than L2 (dataset shard {shard_mb:.0f} MiB "
+                                 f"> 126 MiB), no flush" if shard_mb > 126 else
+                                 f"dataset shard {shard_mb:.0f} MiB fits in the 126 MiB L2 "
+                                 f"(no flush): not an HBM measurement"},
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak,
+                             "unit": "GB/s", "frac": achieved / peak,
+                             "traffic": profile_traffic(aa, n_shard),
+                             "peak_kind": peak_kind, "kernel": "knn_scan_kernel",
+                             "kernel_ms": r["scan_ms"], "merge_ms": r["merge_ms"],
+                             "algorithmic_bytes_per_launch": n_shard * a.dim * 2},
+                "cpu_baseline": cpu,
+                "e2e": {"value": r["e2e"], "unit": UNIT, "h2d_bytes_per_step": nq * a.dim * 4,
+                        "d2h_bytes_per_step": nq * k * 8},
+                "latency": {
+                    "e2e_p50_ms": nearest_rank(r["lat_e2e"], 50),
+                    "e2e_p99_ms": nearest_rank(r["lat_e2e"], 99),
+                    "device_p50_ms": nearest_rank(r["lat_dev"], 50),
+                    "device_p99_ms": nearest_rank(r["lat_dev"], 99),
+                    "samples": a.steps,
+                    "how": "one batch at a time; e2e = host clock around the blocking search "
+                           "with pinned host buffers; device = CUDA events around one "
+                           "device-resident search; max over ranks per sample; nearest rank"},
+                "parity": parity_of(r, nq, k),
+                "gpu_launches": r["launches_total"],
+                "clocks": clk.summary(),
+            }
+            if a.sweep:
+                line["sweep"] = a.sweep
+            line.update(extra)
+            emit(line)
     idx.close()
     if world > 1:
         dist.barrier()

@@ -264,7 +264,8 @@ struct knn_index {
     const void* queries;
     const void* neighbors;
     const void* distances;
-    int in_place;  // bit 0: queries, bit 1: outputs used in place (page-locked host memory)
+    int in_place;  // bit 0: queries, bit 1: outputs used in place (page-locked host memory),
+                   // bit 2: internal-order lists (knn_index_search_lists)
     int64_t nq, k, ks;
     bool i64;
     cudaStream_t stream;
@@ -275,6 +276,10 @@ struct knn_index {
   bool use_graphs = true;
   uint64_t generation = 1;
   std::vector<GraphEntry> graphs;
+
+  // set for the duration of knn_index_search_lists: results stay in the
+  // internal order (inner product: -q.x ascending) for a later merge
+  bool lists_mode = false;
 
   // profiling: one (before scan, after scan, after merge) event triple per
   // search, read back when the stats are requested
@@ -578,7 +583,7 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
   p.pilot_out = nullptr;
   p.thr_init = nullptr;
   p.bound = nullptr;
-  const bool neg = h->metric == KNN_METRIC_INNER_PRODUCT;
+  const bool neg = h->metric == KNN_METRIC_INNER_PRODUCT && !h->lists_mode;
 
   if (prof) KNN_CUDA(cudaEventRecord((*prof)[0], h->stream));
   // with timing events between kernels, launch them plainly serialised
@@ -720,7 +725,7 @@ int search_pass(knn_index* h, const float* queries, int64_t nq, int64_t k, int64
   if (!n_pin) d_pin = nullptr;
   // which host buffers are used in place (a graph key: a buffer that is no
   // longer page-locked must not be replayed into)
-  const int in_place = (q_pin ? 1 : 0) | (d_pin ? 2 : 0);
+  const int in_place = (q_pin ? 1 : 0) | (d_pin ? 2 : 0) | (h->lists_mode ? 4 : 0);
 
   // scratch: everything is sized before any work is enqueued or captured
   const size_t qk = static_cast<size_t>(nq) * k;
@@ -877,11 +882,19 @@ direct:
 // A blocking re-ranked search on one device whose result is not certified
 // for some query is repeated once with the largest candidate count.
 int search_impl(knn_index* h, const float* queries, int64_t nq, int64_t k, void* neighbors,
-                float* distances, bool out_i64, bool sync, bool require_device) {
+                float* distances, bool out_i64, bool sync, bool require_device,
+                bool lists = false) {
   int st = validate_search(h, queries, nq, k, neighbors, distances);
   if (st != KNN_OK || nq == 0 || k == 0) return st;
   std::lock_guard<std::mutex> lock(h->mu);
   KNN_CUDA(cudaSetDevice(h->device));
+  if (lists && h->comm)
+    return fail(KNN_EINVAL, "knn_index_search_lists: the index has a communicator attached");
+  struct ListsMode {
+    knn_index* h;
+    ~ListsMode() { h->lists_mode = false; }
+  } lists_guard{h};
+  h->lists_mode = lists;
 
   const int cq = classify(queries, h->device);
   const int cn = classify(neighbors, h->device);
@@ -982,6 +995,61 @@ int build_impl(knn_index* h, const void* rows, int dtype, int64_t n, int64_t dim
     }
     stage.release();
   }
+  KNN_CUDA(cudaStreamSynchronize(h->stream));
+  int st = encode_rows(&h->xmap, h->data, n, ld, knn::kTileRows);
+  if (st == KNN_OK) st = encode_rows(&h->xmap_tail, h->data, n, ld, knn::kTailBox);
+  if (st != KNN_OK) return st;
+  ++h->generation;
+  drop_graphs(h);
+  h->n = n;
+  h->dim = dim;
+  h->ld = ld;
+  h->metric = metric;
+  h->row_offset = row_offset;
+  h->total_rows = total_rows;
+  return KNN_OK;
+}
+
+// Builds the index from rows already in the engine's storage format: fp16
+// rows (host or device, n x dim, dense) and their fp32 norms as a previous
+// build computed them (knn_index_device_norms); nothing is converted.
+int build_prepared_impl(knn_index* h, const void* rows16, const float* norms, int64_t n,
+                        int64_t dim, int metric, int64_t row_offset, int64_t total_rows) {
+  if (!h) return fail(KNN_EINVAL, "null index");
+  if (metric != KNN_METRIC_L2_EXPANDED && metric != KNN_METRIC_INNER_PRODUCT)
+    return fail(KNN_EINVAL, "metric %d is not L2Expanded (0) or InnerProduct (1)", metric);
+  if (!rows16 || !norms || n <= 0 || dim <= 0)
+    return fail(KNN_EINVAL, "build requires a non-empty dataset and its norms");
+  if (row_offset < 0 || total_rows < row_offset + n)
+    return fail(KNN_EINVAL, "shard [%lld, %lld) outside %lld rows", (long long)row_offset,
+                (long long)(row_offset + n), (long long)total_rows);
+  if (total_rows >= static_cast<int64_t>(KNN_NO_INDEX))
+    return fail(KNN_EUNSUPPORTED, "at most 2^32 - 2 rows (uint32 neighbour indices)");
+  if (n > (int64_t(1) << 31) - 256)
+    return fail(KNN_EUNSUPPORTED, "at most 2^31 - 256 rows per device");
+  if (dim > (int64_t(1) << 20)) return fail(KNN_EUNSUPPORTED, "dim above 2^20");
+  std::lock_guard<std::mutex> lock(h->mu);
+  KNN_CUDA(cudaSetDevice(h->device));
+  if (classify(rows16, h->device) < 0 || classify(norms, h->device) < 0)
+    return fail(KNN_EINVAL, "dataset lives on a different device than the index");
+  if (h->rerank)
+    return fail(KNN_EINVAL, "re-ranking keeps the fp32 rows: build from fp32 rows");
+  if (h->data) cudaFree(h->data);
+  if (h->norms) cudaFree(h->norms);
+  if (h->rows32) cudaFree(h->rows32);
+  h->data = nullptr;
+  h->norms = nullptr;
+  h->rows32 = nullptr;
+  h->n = 0;
+  const int64_t ld = row_ld(dim);
+  KNN_CUDA(cudaMalloc(&h->data, static_cast<size_t>(n) * ld * 2));
+  KNN_CUDA(cudaMalloc(&h->norms, static_cast<size_t>(n) * 4));
+  if (ld != dim) KNN_CUDA(cudaMemsetAsync(h->data, 0, static_cast<size_t>(n) * ld * 2, h->stream));
+  KNN_CUDA(cudaMemcpy2DAsync(h->data, static_cast<size_t>(ld) * 2, rows16,
+                             static_cast<size_t>(dim) * 2, static_cast<size_t>(dim) * 2,
+                             static_cast<size_t>(n), cudaMemcpyDefault, h->stream));
+  KNN_CUDA(cudaMemcpyAsync(h->norms, norms, static_cast<size_t>(n) * 4, cudaMemcpyDefault,
+                           h->stream));
   KNN_CUDA(cudaStreamSynchronize(h->stream));
   int st = encode_rows(&h->xmap, h->data, n, ld, knn::kTileRows);
   if (st == KNN_OK) st = encode_rows(&h->xmap_tail, h->data, n, ld, knn::kTailBox);
@@ -1323,6 +1391,31 @@ int knn_index_copy_rows(knn_index* h, void* out, int dtype) {
   return KNN_OK;
 }
 
+int knn_index_build_prepared(knn_index* h, const void* rows_f16, const float* norms,
+                             int64_t n, int64_t dim, int metric, int64_t row_offset,
+                             int64_t total_rows) {
+  return build_prepared_impl(h, rows_f16, norms, n, dim, metric, row_offset, total_rows);
+}
+
+int knn_index_device_rows(knn_index* h, const void** rows_f16, int64_t* ld) {
+  if (!h || !rows_f16 || !ld) return fail(KNN_EINVAL, "null index or output");
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (!h->data) return fail(KNN_EINVAL, "index has no dataset");
+  *rows_f16 = h->data;
+  *ld = h->ld;
+  return KNN_OK;
+}
+
+int knn_index_device_norms(knn_index* h, const float** norms) {
+  if (!h || !norms) return fail(KNN_EINVAL, "null index or output");
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (!h->data) return fail(KNN_EINVAL, "index has no dataset");
+  *norms = h->norms;
+  return KNN_OK;
+}
+
+int knn_index_device(const knn_index* h) { return h ? h->device : -1; }
+
 int64_t knn_index_rows(const knn_index* h) { return h ? h->n : 0; }
 int64_t knn_index_dim(const knn_index* h) { return h ? h->dim : 0; }
 
@@ -1339,6 +1432,37 @@ int knn_index_search_i64(knn_index* h, const float* queries, int64_t nq, int64_t
 int knn_index_search_async(knn_index* h, const float* queries, int64_t nq, int64_t k,
                            uint32_t* neighbors, float* distances) {
   return search_impl(h, queries, nq, k, neighbors, distances, false, false, true);
+}
+
+int knn_index_search_lists(knn_index* h, const float* queries, int64_t nq, int64_t k,
+                           uint32_t* list_i, float* list_d) {
+  return search_impl(h, queries, nq, k, list_i, list_d, false, false, true, true);
+}
+
+int knn_merge_lists(int device, void* stream, const float* lists_d, const uint32_t* lists_i,
+                    int n_lists, int64_t nq, int64_t k, int metric, void* neighbors,
+                    int neighbors_i64, float* distances) {
+  if (n_lists <= 0 || nq < 0 || k < 0 || k > KNN_MAX_K)
+    return fail(KNN_EINVAL, "knn_merge_lists: n_lists %d, n_queries %lld, k %lld", n_lists,
+                (long long)nq, (long long)k);
+  if (metric != KNN_METRIC_L2_EXPANDED && metric != KNN_METRIC_INNER_PRODUCT)
+    return fail(KNN_EINVAL, "metric %d is not L2Expanded (0) or InnerProduct (1)", metric);
+  if (nq == 0 || k == 0) return KNN_OK;
+  if (!lists_d || !lists_i || !neighbors || !distances)
+    return fail(KNN_EINVAL, "knn_merge_lists: null buffer");
+  KNN_CUDA(cudaSetDevice(device));
+  for (const void* p : {static_cast<const void*>(lists_d), static_cast<const void*>(lists_i),
+                        static_cast<const void*>(neighbors), static_cast<const void*>(distances)})
+    if (classify(p, device) != 1)
+      return fail(KNN_EINVAL, "knn_merge_lists: every buffer must be memory of device %d", device);
+  const int64_t per = nq * k;
+  KNN_CUDA(knn::launch_merge(lists_d, lists_i, per, k, n_lists, static_cast<int>(k), nq, 0,
+                             distances, neighbors, neighbors_i64 != 0,
+                             static_cast<cudaStream_t>(stream),
+                             false, nullptr, metric == KNN_METRIC_INNER_PRODUCT, nullptr,
+                             per * n_lists));
+  g_dispatch.fetch_add(1);
+  return KNN_OK;
 }
 
 int knn_index_sync(knn_index* h) {

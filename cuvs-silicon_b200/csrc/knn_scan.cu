@@ -461,9 +461,14 @@ __device__ __forceinline__ void flush_buffer(RowState<kReg>& st, const Smem& sm,
 // distance R bounds the query's k-th distance over the whole shard (this
 // unit alone has k rows at d <= R), so the CTA publishes R with atomicMin
 // and every CTA filters with the smallest published R from its next tile
-// on.  A row of the final top-k lies at d <= R and still passes in its own
-// unit, whose best k then include it; units may end with fewer than k
-// entries (padding), which the merge ignores.
+// on.  The seed threshold t of a unit's first tile bounds it the same way
+// (k distinct rows of the unit lie at d <= t) and is published as soon as it
+// is known, a tile before any top-k is full.  A row of the final top-k lies
+// at d <= R and still passes in its own unit, whose best k then include it;
+// units may end with fewer than k entries (padding), which the merge ignores.
+// Survivors of a 16-column group are appended one per lane per round (the
+// lowest remaining column first), so a group costs as many rounds as its
+// busiest lane has survivors, usually one.
 template <int kMetric, bool kReg>
 __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base, int warp,
                          int lane) {
@@ -571,7 +576,16 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
 #pragma unroll
             for (int j = 1; j < 32; ++j) tk = fmaxf(tk, j < k ? g[j] : g[0]);
             // keep d <= tk: the next float up
-            if (valid_q && tk < kInf) st.thr = fminf(st.thr, next_up(tk));
+            if (valid_q && tk < kInf) {
+              st.thr = fminf(st.thr, next_up(tk));
+              // this unit holds k distinct rows at d <= tk, so tk bounds the
+              // query's k-th distance over the shard: share it now
+              const uint32_t bits = dist_order_bits(tk);
+              if (p.bound && bits < st.pub && in_bounds(q < p.n_queries, p.err)) {
+                atomicMin(p.bound + q, bits);
+                st.pub = bits;
+              }
+            }
           }
         }
         // One 32-column chunk: distances, threshold filter, survivor buffer.
@@ -599,12 +613,19 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
 #pragma unroll
                 for (int j = 0; j < kRowBuf; ++j) mask |= (dv[h + j] < st.thr ? 1u : 0u) << j;
               }
+              // one survivor per lane per round, lowest column first; the
+              // value is picked by an unrolled select chain (no local memory)
+              uint32_t m = mask;
+              while (__any_sync(0xffffffffu, m != 0)) {
+                if (m != 0) {
+                  const int j = __ffs(m) - 1;
+                  float v = dv[h];
 #pragma unroll
-              for (int j = 0; j < kRowBuf; ++j) {
-                if ((mask >> j) & 1u) {
+                  for (int jj = 1; jj < kRowBuf; ++jj) v = j == jj ? dv[h + jj] : v;
                   if (in_bounds(st.cnt < kRowBuf, p.err))
-                    sm.buf[st.cnt * stride + row] = make_key<kMetric>(dv[h + j], col0 + h + j);
+                    sm.buf[st.cnt * stride + row] = make_key<kMetric>(v, col0 + h + j);
                   ++st.cnt;
+                  m &= m - 1u;
                 }
               }
             }

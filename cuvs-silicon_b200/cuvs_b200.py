@@ -87,6 +87,12 @@ def lib() -> ctypes.CDLL:
         "knn_index_set_graphs": (I, [P, I]),
         "knn_index_set_peer_exchange": (I, [P, I]),
         "knn_index_set_peer_timeout": (I, [P, I64]),
+        "knn_index_device": (I, [P]),
+        "knn_index_device_rows": (I, [P, ctypes.POINTER(P), ctypes.POINTER(I64)]),
+        "knn_index_device_norms": (I, [P, ctypes.POINTER(P)]),
+        "knn_index_build_prepared": (I, [P, P, P, I64, I64, I, I64, I64]),
+        "knn_index_search_lists": (I, [P, P, I64, I64, P, P]),
+        "knn_merge_lists": (I, [I, P, P, P, I, I64, I64, I, P, I, P]),
         "knn_index_kernel_stats": (I, [P, ctypes.POINTER(ctypes.c_double),
                                        ctypes.POINTER(ctypes.c_double),
                                        ctypes.POINTER(I64), ctypes.POINTER(I64)]),

@@ -143,6 +143,28 @@ int knn_index_build_file(knn_index* index, const char* path, int format, int met
 
 int64_t knn_index_rows(const knn_index* index);
 int64_t knn_index_dim(const knn_index* index);
+/* The CUDA device the index lives on (-1 for a null index). */
+int knn_index_device(const knn_index* index);
+
+/* The index's device cache, the state the reference's MetalContext keeps for
+ * a dataset (src/metal_context.mm:38-54,155-175: the fp16 copy of the rows
+ * and the fp32 d_norms), owned here by the index: the fp16 rows (n_rows rows
+ * of `ld` halves each, the first dim of them the values, the rest zero) and
+ * the fp32 squared norms of those fp16 rows (n_rows floats).  Device
+ * pointers, valid until the index is rebuilt or destroyed; read only. */
+int knn_index_device_rows(knn_index* index, const void** rows_f16, int64_t* ld);
+int knn_index_device_norms(knn_index* index, const float** norms);
+
+/* Builds the index (or one row shard, as knn_index_build_shard) from rows
+ * already in the engine's storage format: fp16 rows (host or device,
+ * n_rows x dim, dense) and the fp32 norms a previous build computed for
+ * them (knn_index_device_norms), as cuvs::neighbors::brute_force::serialize
+ * stores them with its fp16 payload.  Nothing is converted or recomputed:
+ * the norms must belong to these rows.  No counterpart in the reference
+ * (its cache is rebuilt from fp32 rows on every first search). */
+int knn_index_build_prepared(knn_index* index, const void* rows_f16, const float* norms,
+                             int64_t n_rows, int64_t dim, int metric, int64_t row_offset,
+                             int64_t total_rows);
 
 /* Copies the index's stored rows (n_rows x dim, row-major, the fp16 values
  * the engine searches) into `out`: dtype KNN_DTYPE_F16 to host or device
@@ -213,6 +235,26 @@ int knn_index_search_async(knn_index* index, const float* queries,
                            float* distances);
 /* Waits for the index's stream and reports device-side errors. */
 int knn_index_sync(knn_index* index);
+
+/* Stream-ordered search of one row shard whose result is merged later with
+ * other shards' (knn_merge_lists): as knn_index_search_async (device
+ * buffers, global row indices), but distances stay in the order the merge
+ * works in: squared L2 ascending, or for the inner product -q.x ascending
+ * (so that ties still go to the smaller index).  The index must not have a
+ * communicator attached.  No counterpart in the reference. */
+int knn_index_search_lists(knn_index* index, const float* queries, int64_t n_queries,
+                           int64_t k, uint32_t* list_neighbors, float* list_distances);
+
+/* Merges n_lists per-shard results of knn_index_search_lists into the
+ * final top-k on device `device`, stream-ordered on `cuda_stream` (NULL:
+ * the legacy default stream).  lists_*: [n_lists][n_queries][k] in device
+ * memory of `device` (copy other devices' lists there first); outputs, in
+ * device memory of `device`, as knn_index_search (inner product: q.x
+ * descending), with int64 neighbours (-1 = none) when neighbors_i64 != 0.
+ * No counterpart in the reference, which searches on one device. */
+int knn_merge_lists(int device, void* cuda_stream, const float* lists_distances,
+                    const uint32_t* lists_neighbors, int n_lists, int64_t n_queries, int64_t k,
+                    int metric, void* neighbors, int neighbors_i64, float* distances);
 
 /* Exact fp32 re-ranking (no counterpart in the reference's Metal path; it
  * makes searches return what the reference's portable exact search,

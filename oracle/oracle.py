@@ -185,6 +185,13 @@ def ref_lib() -> ctypes.CDLL:
     lib.ref_cagra_build_inner_product.restype = ctypes.c_int
     lib.ref_cagra_build_inner_product.argtypes = [
         ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64]
+    lib.ref_cagra_save_index.restype = ctypes.c_int
+    lib.ref_cagra_save_index.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                         ctypes.c_char_p]
+    lib.ref_cagra_load_search.restype = ctypes.c_int
+    lib.ref_cagra_load_search.argtypes = [
+        ctypes.c_char_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+        ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)]
     lib.ref_squared_l2_distance_128.restype = ctypes.c_float
     lib.ref_squared_l2_distance_128.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
     lib.ref_last_error.restype = ctypes.c_char_p
@@ -248,6 +255,32 @@ def ref_knn(base, queries, k, threads: int = 1):
         raise ValueError("reference search failed: "
                          + lib.ref_last_error().decode(errors="replace"))
     return idx, dist
+
+
+def ref_save_index(base, path: str) -> None:
+    """The reference's cagra::build + cagra::save_index (src/cagra.cpp:268-328)."""
+    base = _c(base, np.float32)
+    lib = ref_lib()
+    if lib.ref_cagra_save_index(base.ctypes.data, base.shape[0], base.shape[1],
+                                path.encode()) != 0:
+        raise ValueError("reference save_index failed: "
+                         + lib.ref_last_error().decode(errors="replace"))
+
+
+def ref_load_search(path: str, queries, k):
+    """The reference's cagra::load_index (src/cagra.cpp:330-366) and its exact
+    search on the loaded index.  Returns (idx, dist, (rows, dim))."""
+    queries = _c(queries, np.float32)
+    nq = queries.shape[0]
+    idx = np.empty((nq, k), dtype=np.uint32)
+    dist = np.empty((nq, k), dtype=np.float32)
+    rows, dim = ctypes.c_int64(), ctypes.c_int64()
+    lib = ref_lib()
+    if lib.ref_cagra_load_search(path.encode(), queries.ctypes.data, nq, k, idx.ctypes.data,
+                                 dist.ctypes.data, ctypes.byref(rows), ctypes.byref(dim)) != 0:
+        raise ValueError("reference load_index/search failed: "
+                         + lib.ref_last_error().decode(errors="replace"))
+    return idx, dist, (rows.value, dim.value)
 
 
 def merge_lists(list_d, list_i, index_offset=None):

@@ -73,6 +73,56 @@ int ref_cagra_build_inner_product(const float* base, std::int64_t n,
   }
 }
 
+// The reference's own container code (src/cagra.cpp:268-366): cagra::build
+// with the dataset attached, then cagra::save_index(path).  Used to check
+// that files written by either side load on the other.
+int ref_cagra_save_index(const float* base, std::int64_t n, std::int64_t dim,
+                         const char* path) {
+  try {
+    raft::resources res;
+    cuvs::neighbors::cagra::index_params ip;
+    ip.metric = cuvs::distance::DistanceType::L2Expanded;
+    ip.graph_degree = 0;
+    auto idx = cuvs::neighbors::cagra::build(
+        res, ip,
+        raft::make_device_matrix_view<const float, std::int64_t>(base, n, dim));
+    cuvs::neighbors::cagra::save_index(idx, path);
+    return 0;
+  } catch (const std::invalid_argument& e) {
+    g_err = e.what();
+    return 1;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return 2;
+  }
+}
+
+// cagra::load_index(path) and the reference's search on the loaded index;
+// *rows / *dim receive the loaded shape.
+int ref_cagra_load_search(const char* path, const float* queries, std::int64_t nq,
+                          std::int64_t k, std::uint32_t* out_idx, float* out_dist,
+                          std::int64_t* rows, std::int64_t* dim) {
+  try {
+    raft::resources res;
+    auto idx = cuvs::neighbors::cagra::load_index(path);
+    *rows = idx.rows();
+    *dim = idx.cols();
+    cuvs::neighbors::cagra::search_params sp;
+    cuvs::neighbors::cagra::search(
+        res, sp, idx,
+        raft::make_device_matrix_view<const float, std::int64_t>(queries, nq, idx.cols()),
+        raft::make_device_matrix_view<std::uint32_t, std::int64_t>(out_idx, nq, k),
+        raft::make_device_matrix_view<float, std::int64_t>(out_dist, nq, k));
+    return 0;
+  } catch (const std::invalid_argument& e) {
+    g_err = e.what();
+    return 1;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return 2;
+  }
+}
+
 // src/distance.cpp:8-20.
 float ref_squared_l2_distance_128(const float* a, const float* b) {
   return cuvs_silicon::squared_l2_distance_128(a, b);

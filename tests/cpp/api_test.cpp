@@ -7,12 +7,17 @@
 //     values :299-396), written here without FAISS;
 //   * the dispatch spy (tests/test_metal_search.cpp:16-58);
 //   * attach_dataset_on_build = false (faiss smoke :247-261);
-// plus save/load round trips, brute_force, and the validation errors of
-// src/cagra.cpp:26-32,100-111.  Exit code 0 = all passed.
+// plus save/load round trips, brute_force (its device cache views, the fp16
+// + norms container payload, an index sharded over the devices of a
+// raft::resources), and the validation errors of src/cagra.cpp:26-32,100-111.
+// Exit code 0 = all passed.
+#include <cuda_runtime.h>
+
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
+#include <fstream>
 #include <functional>
 #include <limits>
 #include <stdexcept>
@@ -292,12 +297,152 @@ static void test_save_load_and_brute_force(const std::string& tmpdir) {
   }));
 }
 
+// IEEE binary16 bits -> float (exact), for checking the device cache.
+static float half_bits_to_float(std::uint16_t h) {
+  const int e = (h >> 10) & 31, m = h & 1023;
+  const float sign = (h & 0x8000) ? -1.0f : 1.0f;
+  if (e == 0) return sign * std::ldexp(static_cast<float>(m), -24);
+  if (e == 31) return m ? std::numeric_limits<float>::quiet_NaN()
+                        : sign * std::numeric_limits<float>::infinity();
+  return sign * std::ldexp(static_cast<float>(m + 1024), e - 25);
+}
+
+// The index's device cache (the reference's fp16 dataset + d_norms,
+// src/metal_context.mm:38-54,155-175) through dataset()/norms(), and the
+// fp16 + norms container payload that reloads without conversion.
+static void test_device_cache_and_fp16_payload(const std::string& tmpdir) {
+  const std::int64_t n = 3001, d = 70, q = 5, k = 9;
+  const auto base = random_rows(n, d, 3);
+  const auto qs = random_rows(q, d, 4);
+  raft::resources res;
+  auto bi = bf::build(res, raft::make_device_matrix_view<const float, std::int64_t>(base.data(), n, d));
+  const auto rows = bi.dataset();
+  const auto norms = bi.norms();
+  EXPECT(rows.rows == n && rows.dim == d && rows.ld >= d && rows.ld % 8 == 0);
+  EXPECT(norms.size() == n);
+  std::vector<std::uint16_t> h16(static_cast<std::size_t>(n * rows.ld));
+  std::vector<float> hn(static_cast<std::size_t>(n));
+  EXPECT(cudaMemcpy(h16.data(), rows.data, h16.size() * 2, cudaMemcpyDeviceToHost) == cudaSuccess);
+  EXPECT(cudaMemcpy(hn.data(), norms.data_handle(), hn.size() * 4, cudaMemcpyDeviceToHost) ==
+         cudaSuccess);
+  int bad_rows = 0, bad_norms = 0;
+  for (std::int64_t r = 0; r < n; ++r) {
+    double acc = 0.0;
+    for (std::int64_t c = 0; c < rows.ld; ++c) {
+      const float v = half_bits_to_float(h16[static_cast<std::size_t>(r * rows.ld + c)]);
+      if (c < d) {
+        // round-to-nearest-even fp16 of the input: within half an fp16 ulp
+        const float x = base[static_cast<std::size_t>(r * d + c)];
+        if (std::fabs(v - x) > std::ldexp(std::fabs(x), -11) + 1e-7f) ++bad_rows;
+        acc += static_cast<double>(v) * v;
+      } else if (v != 0.0f) {
+        ++bad_rows;  // padding columns are zero
+      }
+    }
+    if (std::fabs(hn[static_cast<std::size_t>(r)] - acc) > 1e-5 * (acc + 1e-6)) ++bad_norms;
+  }
+  EXPECT(bad_rows == 0 && bad_norms == 0);
+
+  std::vector<std::int64_t> l1(q * k), l2(q * k);
+  std::vector<float> d1(q * k), d2(q * k);
+  bf::search(res, bi, raft::make_device_matrix_view<const float, std::int64_t>(qs.data(), q, d),
+             raft::make_device_matrix_view<std::int64_t, std::int64_t>(l1.data(), q, k),
+             raft::make_device_matrix_view<float, std::int64_t>(d1.data(), q, k));
+  const std::string path = tmpdir + "/bf_fp16.bin";
+  bf::serialize(res, path, bi, bf::payload::fp16_with_norms);
+  {
+    std::ifstream f(path, std::ios::binary | std::ios::ate);
+    EXPECT(static_cast<std::int64_t>(f.tellg()) == 32 + n * d * 2 + n * 4);
+  }
+  auto bl = bf::deserialize(res, path);
+  EXPECT(bl.size() == n && bl.dim() == d);
+  bf::search(res, bl, raft::make_device_matrix_view<const float, std::int64_t>(qs.data(), q, d),
+             raft::make_device_matrix_view<std::int64_t, std::int64_t>(l2.data(), q, k),
+             raft::make_device_matrix_view<float, std::int64_t>(d2.data(), q, k));
+  EXPECT(l1 == l2 && d1 == d2);
+  // the reloaded cache holds the same norms, bit for bit
+  std::vector<float> hn2(static_cast<std::size_t>(n));
+  EXPECT(cudaMemcpy(hn2.data(), bl.norms().data_handle(), hn2.size() * 4,
+                    cudaMemcpyDeviceToHost) == cudaSuccess);
+  EXPECT(hn2 == hn);
+  // the reference's loader sees no fp32 dataset block in an fp16 file
+  auto as_cagra = cg::load_index(path);
+  EXPECT(as_cagra.rows() == n && as_cagra.dataset().empty());
+}
+
+// A raft::resources with several devices shards the index across them; the
+// merged result equals the single-device index's byte for byte.  With one
+// GPU the device list {0, 0} still runs two shards, streams, the gather and
+// the device merge.
+static void test_multi_device_index(const std::string& tmpdir) {
+  int count = 0;
+  cudaGetDeviceCount(&count);
+  const std::vector<int> devs = count >= 2 ? std::vector<int>{0, 1} : std::vector<int>{0, 0};
+  const std::int64_t n = 20011, d = 72, q = 37, k = 10;
+  const auto base = random_rows(n, d, 5);
+  const auto qs = random_rows(q, d, 6);
+  raft::resources one;
+  raft::resources multi(devs);
+  EXPECT(multi.devices().size() == 2 && multi.device() == 0);
+  for (auto metric : {cuvs::distance::DistanceType::L2Expanded,
+                      cuvs::distance::DistanceType::InnerProduct}) {
+    auto single = bf::build(one, raft::make_device_matrix_view<const float, std::int64_t>(base.data(), n, d), metric);
+    auto sharded = bf::build(multi, raft::make_device_matrix_view<const float, std::int64_t>(base.data(), n, d), metric);
+    EXPECT(sharded.n_shards() == 2 && sharded.size() == n);
+    EXPECT(sharded.shard_row_offset(1) == sharded.shard_rows(0));
+    EXPECT(sharded.shard_device(1) == devs[1]);
+    for (std::int64_t kk : {std::int64_t(1), k, std::int64_t(100)}) {
+      std::vector<std::int64_t> l1(q * kk), l2(q * kk);
+      std::vector<std::uint32_t> u2(q * kk);
+      std::vector<float> d1(q * kk), d2(q * kk), e2(q * kk);
+      auto qv = raft::make_device_matrix_view<const float, std::int64_t>(qs.data(), q, d);
+      bf::search(one, single, qv, raft::make_device_matrix_view<std::int64_t, std::int64_t>(l1.data(), q, kk),
+                 raft::make_device_matrix_view<float, std::int64_t>(d1.data(), q, kk));
+      bf::search(multi, sharded, qv, raft::make_device_matrix_view<std::int64_t, std::int64_t>(l2.data(), q, kk),
+                 raft::make_device_matrix_view<float, std::int64_t>(d2.data(), q, kk));
+      bf::search(multi, sharded, qv, raft::make_device_matrix_view<std::uint32_t, std::int64_t>(u2.data(), q, kk),
+                 raft::make_device_matrix_view<float, std::int64_t>(e2.data(), q, kk));
+      EXPECT(l1 == l2 && d1 == d2 && d1 == e2);
+      for (std::int64_t i = 0; i < q * kk; ++i) EXPECT(static_cast<std::int64_t>(u2[i]) == l1[i]);
+    }
+  }
+  // device-resident queries and outputs, and a sharded fp16 round trip
+  auto sharded = bf::build(multi, raft::make_device_matrix_view<const float, std::int64_t>(base.data(), n, d));
+  float* dq = nullptr;
+  std::int64_t* dl = nullptr;
+  float* dd = nullptr;
+  cudaSetDevice(0);
+  EXPECT(cudaMalloc(&dq, q * d * 4) == cudaSuccess && cudaMalloc(&dl, q * k * 8) == cudaSuccess &&
+         cudaMalloc(&dd, q * k * 4) == cudaSuccess);
+  cudaMemcpy(dq, qs.data(), q * d * 4, cudaMemcpyHostToDevice);
+  bf::search(multi, sharded, raft::make_device_matrix_view<const float, std::int64_t>(dq, q, d),
+             raft::make_device_matrix_view<std::int64_t, std::int64_t>(dl, q, k),
+             raft::make_device_matrix_view<float, std::int64_t>(dd, q, k));
+  std::vector<std::int64_t> l3(q * k), l4(q * k);
+  std::vector<float> d3(q * k), d4(q * k);
+  cudaMemcpy(l3.data(), dl, q * k * 8, cudaMemcpyDeviceToHost);
+  cudaMemcpy(d3.data(), dd, q * k * 4, cudaMemcpyDeviceToHost);
+  cudaFree(dq);
+  cudaFree(dl);
+  cudaFree(dd);
+  const std::string path = tmpdir + "/bf_sharded.bin";
+  bf::serialize(multi, path, sharded, bf::payload::fp16_with_norms);
+  auto back = bf::deserialize(multi, path);
+  EXPECT(back.n_shards() == 2);
+  bf::search(multi, back, raft::make_device_matrix_view<const float, std::int64_t>(qs.data(), q, d),
+             raft::make_device_matrix_view<std::int64_t, std::int64_t>(l4.data(), q, k),
+             raft::make_device_matrix_view<float, std::int64_t>(d4.data(), q, k));
+  EXPECT(l3 == l4 && d3 == d4);
+}
+
 int main(int argc, char** argv) {
   const std::string tmpdir = argc > 1 ? argv[1] : "/tmp";
   test_faiss_adapter_values();
   test_dispatch_spy();
   test_lifecycle_and_validation();
   test_save_load_and_brute_force(tmpdir);
+  test_device_cache_and_fp16_payload(tmpdir);
+  test_multi_device_index(tmpdir);
   if (g_failures) {
     std::fprintf(stderr, "%d expectation(s) failed\n", g_failures);
     return 1;
