@@ -567,8 +567,11 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
   p.err = h->err_dev;
   p.n_rows = h->n;
   p.n_queries = nq;
-  p.n_gran = (h->n + knn::kGranRows - 1) / knn::kGranRows;
+  p.n_gran = (h->n + plan.gran_rows - 1) / plan.gran_rows;
   p.q_rows = nq_pad;
+  p.pair = static_cast<int32_t>(plan.pair);
+  p.gran_rows = static_cast<int32_t>(plan.gran_rows);
+  p.unit_queries = static_cast<int32_t>(plan.unit_queries);
   p.ld = h->ld;
   p.k = static_cast<int32_t>(ks);
   p.query_block = static_cast<int32_t>(plan.query_block);
@@ -1527,6 +1530,8 @@ int knn_plan_search(int64_t n_rows, int64_t dim, int64_t nq, int64_t k, int num_
   out->stages = p.stages;
   out->smem_bytes = p.smem_bytes;
   out->partial_bytes = p.partial_bytes;
+  out->pair = p.pair;
+  out->unit_queries = p.unit_queries;
   return KNN_OK;
 }
 
@@ -1783,8 +1788,11 @@ int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
   p.err = h->err_dev;
   p.n_rows = h->n;
   p.n_queries = nq;
-  p.n_gran = (h->n + knn::kGranRows - 1) / knn::kGranRows;
+  p.n_gran = (h->n + plan.gran_rows - 1) / plan.gran_rows;
   p.q_rows = nq_pad;
+  p.pair = static_cast<int32_t>(plan.pair);
+  p.gran_rows = static_cast<int32_t>(plan.gran_rows);
+  p.unit_queries = static_cast<int32_t>(plan.unit_queries);
   p.ld = h->ld;
   p.k = static_cast<int32_t>(k);
   p.query_block = static_cast<int32_t>(plan.query_block);

@@ -48,6 +48,12 @@ struct ScanParams {
   int64_t n_gran;  // ceil(n_rows / kGranRows)
   int64_t q_rows;  // rows of the fp16 query buffer (padded_query_rows)
   int64_t ld;      // leading dimension of the fp16 rows and queries (halves)
+  // CTA pairs (pair = 1): clusters of two CTAs share each dataset tile
+  // (cta_group::2 MMAs, M = 256); a unit then covers 256 query rows, 128
+  // per CTA.  Work units split the rows in granules of gran_rows.
+  int32_t pair;
+  int32_t gran_rows;     // kGranRows, or 2 * kGranRows with pairs
+  int32_t unit_queries;  // query rows of a unit: query_block, or 256 with pairs
   int32_t k;
   int32_t query_block;  // query rows owned per work unit (multiple of 32, <= 128)
   int32_t query_tiles;
@@ -80,6 +86,7 @@ cudaError_t launch_pilot_threshold(const float* pilot, int splits, int k, int64_
 struct Plan {
   int64_t query_block, query_tiles, row_tiles, splits, units, grid, stages;
   int64_t smem_bytes, partial_bytes;
+  int64_t pair = 0, gran_rows = kGranRows, unit_queries = 0;
 };
 
 // Returns 0 and fills `out`, or a KNN_E* status (KNN_EUNSUPPORTED when k is
@@ -112,6 +119,7 @@ cudaError_t launch_convert_rows(const void* in, bool in_is_half, int64_t rows,
 // Rows of the fp16 query buffer a search needs: every 128-row query slab
 // the scan kernel loads lies inside it, so no TMA box leaves the buffer.
 inline int64_t padded_query_rows(const Plan& plan) {
+  if (plan.pair) return plan.query_tiles * 2 * kQueryRows;
   return (plan.query_tiles - 1) * plan.query_block + kQueryRows;
 }
 

@@ -43,6 +43,11 @@ constexpr int kStageEntries = 6144;  // 48 KiB of (fp32, uint32) entries (fold p
 constexpr int kSelCap = 2048;        // lists' j-th entries (threshold path)
 constexpr int kCandCap = 4096;       // threshold-path candidates
 constexpr int kRankPlaceMax = 1024;  // candidates ordered by rank counting (4 per thread)
+// Lists longer than this: prefix lengths by binary search, candidates copied
+// by the whole block, and rank counting only up to kRankPlaceLong of them
+// (it is quadratic; the block-wide sort takes over above).
+constexpr int kLongList = 128;
+constexpr int kRankPlaceLong = 256;
 static_assert(kSelCap + kCandCap <= kStageEntries, "threshold arrays share the stage");
 
 __device__ __forceinline__ bool less_pair(float da, uint32_t ia, float db, uint32_t ib) {
@@ -437,7 +442,56 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
   // tau is the padding, i.e. when fewer than r lists have j entries)
   const int total = n_lists * k;
   constexpr int kPer = 8;  // entries per thread per round, loaded before use
-  if (n_lists <= static_cast<int>(blockDim.x)) {
+  if (n_lists <= static_cast<int>(blockDim.x) && k > kLongList) {
+    // Long lists: thread l finds the length of list l's prefix <= tau by
+    // binary search (about log2 k dependent loads instead of a walk of up to
+    // k), a block scan turns the lengths into offsets, and all threads copy
+    // the candidates together.  The offsets reuse the selection array
+    // (tau is already in registers).
+    int* off = reinterpret_cast<int*>(seli);  // [n_lists + 1]
+    int len = 0;
+    if (tid < n_lists) {
+      const float* lsd = qd + static_cast<int64_t>(tid) * stride_list;
+      const uint32_t* lsi = qi + static_cast<int64_t>(tid) * stride_list;
+      int lo = 0, hi = k;  // entries [0, lo) are <= tau, [hi, k) are not
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        const float dm = lsd[mid];
+        const uint32_t im = lsi[mid];
+        if (im != kNoIndex && (dm < td || (dm == td && im <= ti))) lo = mid + 1;
+        else hi = mid;
+      }
+      len = lo;
+    }
+    // exclusive scan of the lengths: warp scans, then the warp totals
+    __shared__ int s_warp[kMergeWarps];
+    int incl = len;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) s_warp[tid >> 5] = incl;
+    __syncthreads();
+    int base = 0;
+    for (int w = 0; w < (tid >> 5); ++w) base += s_warp[w];
+    if (tid < n_lists) off[tid] = base + incl - len;
+    if (tid == static_cast<int>(blockDim.x) - 1) s_count = base + incl;
+    __syncthreads();
+    const int cnt = s_count < kCandCap ? s_count : kCandCap;
+    for (int c = tid; c < cnt; c += blockDim.x) {
+      // list of candidate c: the last l with off[l] <= c
+      int a = 0, b = n_lists - 1;
+      while (a < b) {
+        const int m = (a + b + 1) >> 1;
+        if (off[m] <= c) a = m;
+        else b = m - 1;
+      }
+      const int64_t at = static_cast<int64_t>(a) * stride_list + (c - off[a]);
+      cd[c] = qd[at];
+      ci[c] = qi[at];
+    }
+  } else if (n_lists <= static_cast<int>(blockDim.x)) {
     // The lists are sorted, so a list's candidates are a prefix of it:
     // thread l reads list l four entries at a time (independent loads) and
     // stops at the first entry above tau or at the padding.
@@ -513,7 +567,7 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
     emit_result(ex, epoch, q, k, cd, ci, k, index_offset, out_d, out_i, sign);
     return;
   }
-  if (count <= kRankPlaceMax) {
+  if (count <= (k > kLongList ? kRankPlaceLong : kRankPlaceMax)) {
     // candidates are distinct (distinct row indices): rank counting places
     // the first k of them, sorted, in front of the selection array
     rank_place(cd, ci, count, seld, seli, k);

@@ -130,12 +130,19 @@ struct Smem {
   uint32_t* tmem_slot;
 };
 
+// Bytes of one pipeline stage: the query slab and the dataset slab (the
+// whole tile's, or with CTA pairs this CTA's half of it).
+__host__ __device__ __forceinline__ int stage_bytes(int pair) {
+  return kStageA + (pair ? kTileRows / 2 : kTileRows) * kKChunk * 2;
+}
+
 __device__ __forceinline__ Smem carve(uint8_t* raw, const ScanParams& p) {
   Smem s;
   const uint32_t base = smem_addr(raw);
   const uint32_t pad = (1024u - (base & 1023u)) & 1023u;
   s.stages = raw + pad;
-  s.heap = reinterpret_cast<uint64_t*>(s.stages + static_cast<size_t>(p.stages) * kStageBytes);
+  s.heap = reinterpret_cast<uint64_t*>(s.stages +
+                                       static_cast<size_t>(p.stages) * stage_bytes(p.pair));
   s.buf = s.heap + static_cast<size_t>(p.k) * p.query_block;
   s.norm_stage = reinterpret_cast<float*>(s.buf + static_cast<size_t>(kRowBuf) * p.query_block);
   uintptr_t b = reinterpret_cast<uintptr_t>(s.norm_stage + 4 * kAccCols);
@@ -162,8 +169,8 @@ __device__ __forceinline__ Unit unit_of(const ScanParams& p, int u) {
   Unit x;
   x.m = u % p.query_tiles;
   const int64_t s = u / p.query_tiles;
-  x.r0 = s * p.n_gran / p.splits * kGranRows;
-  x.r_end = (s + 1) * p.n_gran / p.splits * kGranRows;
+  x.r0 = s * p.n_gran / p.splits * p.gran_rows;
+  x.r_end = (s + 1) * p.n_gran / p.splits * p.gran_rows;
   if (p.pilot && x.r_end > x.r0 + kTileRows) x.r_end = x.r0 + kTileRows;
   return x;
 }
@@ -192,36 +199,58 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
 // boxes of 32 rows placed one after the other, which gives the same
 // shared-memory layout for its first w rows (every box starts on a 1024-byte
 // swizzle atom).
+template <bool kPair>
 __device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap,
                          const CUtensorMap* xmap_tail, const ScanParams& p, const Smem& sm) {
   const uint64_t pol_q = policy_evict_last();
   const uint64_t pol_x = p.dataset_evict_first ? policy_evict_first() : policy_evict_normal();
-  auto load_rows = [&](uint8_t* dst, uint64_t* bar, int kc, int64_t rs, int w) {
+  const uint32_t crank = kPair ? cluster_ctarank() : 0u;
+  const int first = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int step = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const int sbytes = stage_bytes(kPair);
+  // With pairs, a tile of w rows is split in two halves of w / 2 rows
+  // (multiples of 32: the granule is 64 rows), this CTA loading half crank;
+  // the loads count on the first CTA's full barrier.
+  auto half_rows = [&](int w) { return kPair ? w / 2 : w; };
+  auto bar_of = [&](uint32_t slot) -> uint32_t {
+    return kPair ? mapa_shared(&sm.full[slot], 0) : smem_addr(&sm.full[slot]);
+  };
+  auto expect = [&](uint32_t slot, uint32_t bytes) {
+    if constexpr (kPair) mbar_arrive_expect_tx_cluster(bar_of(slot), bytes);
+    else mbar_arrive_expect_tx(&sm.full[slot], bytes);
+  };
+  auto load = [&](void* dst, const CUtensorMap* map, uint32_t slot, int32_t x, int32_t y,
+                  uint64_t pol) {
+    if constexpr (kPair) tma_load_2d_pair(dst, map, bar_of(slot), x, y, pol);
+    else tma_load_2d(dst, map, &sm.full[slot], x, y, pol);
+  };
+  auto load_rows = [&](uint8_t* dst, uint32_t slot, int kc, int64_t rs, int w) {
+    const int h = half_rows(w);
+    const int64_t r0 = rs + (kPair ? static_cast<int64_t>(crank) * h : 0);
     // rows past n_rows (less than a granule) are TMA's zero fill
-    if (!in_bounds(rs >= 0 && rs < p.n_rows && w > 0 && w <= kTileRows && w % kTailBox == 0 &&
-                       kc * kKChunk < p.ld,
+    if (!in_bounds(r0 >= 0 && r0 < p.n_rows + p.gran_rows && w > 0 && w <= kTileRows &&
+                       h % kTailBox == 0 && kc * kKChunk < p.ld,
                    p.err))
       return;
-    if (w == kTileRows) {
-      tma_load_2d(dst, xmap, bar, kc * kKChunk, static_cast<int32_t>(rs), pol_x);
+    if (!kPair && w == kTileRows) {
+      load(dst, xmap, slot, kc * kKChunk, static_cast<int32_t>(r0), pol_x);
     } else {
-      for (int j = 0; j < w; j += kTailBox)
-        tma_load_2d(dst + j * (kKChunk * 2), xmap_tail, bar, kc * kKChunk,
-                    static_cast<int32_t>(rs + j), pol_x);
+      for (int j = 0; j < h; j += kTailBox)
+        load(dst + j * (kKChunk * 2), xmap_tail, slot, kc * kKChunk,
+             static_cast<int32_t>(r0 + j), pol_x);
     }
   };
   // phase 1: dataset slabs of the first p.stages loads (every stage is free)
   uint32_t pre = 0;
-  for (int u = blockIdx.x; u < p.units && pre < static_cast<uint32_t>(p.stages);
-       u += gridDim.x) {
+  for (int u = first; u < p.units && pre < static_cast<uint32_t>(p.stages); u += step) {
     const Unit un = unit_of(p, u);
     for (int64_t rs = un.r0; rs < un.r_end && pre < static_cast<uint32_t>(p.stages);
          rs += kTileRows) {
       const int w = tile_width(rs, un.r_end);
       for (int kc = 0; kc < p.k_chunks && pre < static_cast<uint32_t>(p.stages); ++kc) {
-        uint8_t* st = sm.stages + static_cast<size_t>(pre) * kStageBytes;
-        mbar_arrive_expect_tx(&sm.full[pre], kStageA + w * (kKChunk * 2));
-        load_rows(st + kStageA, &sm.full[pre], kc, rs, w);
+        uint8_t* st = sm.stages + static_cast<size_t>(pre) * sbytes;
+        expect(pre, kStageA + half_rows(w) * (kKChunk * 2));
+        load_rows(st + kStageA, pre, kc, rs, w);
         ++pre;
       }
     }
@@ -230,9 +259,9 @@ __device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap,
   // phase 2: every load in order; the first `pre` only need their query slab
   uint32_t it = 0;
   bool failed = false;
-  for (int u = blockIdx.x; u < p.units && !failed; u += gridDim.x) {
+  for (int u = first; u < p.units && !failed; u += step) {
     const Unit un = unit_of(p, u);
-    const int32_t qy = un.m * p.query_block;
+    const int32_t qy = un.m * p.unit_queries + static_cast<int32_t>(crank) * kQueryRows;
     if (!in_bounds(qy >= 0 && qy + kQueryRows <= p.q_rows, p.err)) {
       failed = true;
       break;
@@ -241,9 +270,9 @@ __device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap,
       const int w = tile_width(rs, un.r_end);
       for (int kc = 0; kc < p.k_chunks; ++kc) {
         const uint32_t slot = it % p.stages;
-        uint8_t* st = sm.stages + static_cast<size_t>(slot) * kStageBytes;
+        uint8_t* st = sm.stages + static_cast<size_t>(slot) * sbytes;
         if (it < pre) {
-          tma_load_2d(st, qmap, &sm.full[slot], kc * kKChunk, qy, pol_q);
+          load(st, qmap, slot, kc * kKChunk, qy, pol_q);
           ++it;
           continue;
         }
@@ -252,30 +281,44 @@ __device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap,
           failed = true;
           break;
         }
-        mbar_arrive_expect_tx(&sm.full[slot], kStageA + w * (kKChunk * 2));
-        tma_load_2d(st, qmap, &sm.full[slot], kc * kKChunk, qy, pol_q);
-        load_rows(st + kStageA, &sm.full[slot], kc, rs, w);
+        expect(slot, kStageA + half_rows(w) * (kKChunk * 2));
+        load(st, qmap, slot, kc * kKChunk, qy, pol_q);
+        load_rows(st + kStageA, slot, kc, rs, w);
         ++it;
       }
     }
   }
-  if (failed) {
-    // Let the copies already issued land before the CTA can retire.
+  if (failed && kPair) {
+    // copies this CTA issued may still be landing in its shared memory:
+    // give them time before the CTA can retire (bounded, 2 ms)
+    const uint64_t t0 = global_timer_ns();
+    while (global_timer_ns() - t0 < 2000000ull) {
+    }
+  }
+  if (failed && !kPair) {
+    // Let the copies already issued land before the CTA can retire.  (With
+    // pairs the copies complete on the first CTA's barrier; both CTAs wait
+    // for each other at the end of the kernel, after bounded waits.)
     const uint32_t outstanding = it < static_cast<uint32_t>(p.stages) ? it : p.stages;
     for (uint32_t j = it - outstanding; j < it; ++j)
       drain_wait(&sm.full[j % p.stages], (j / p.stages) & 1u);
   }
 }
 
+template <bool kPair>
 __device__ void mma_issuer(const ScanParams& p, const Smem& sm, uint32_t tmem_base) {
+  // with pairs only the first CTA issues; the MMAs read both CTAs' slabs
+  const int first = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int step = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const int sbytes = stage_bytes(kPair);
   uint32_t it = 0, tc = 0;
   bool failed = false;
-  for (int u = blockIdx.x; u < p.units && !failed; u += gridDim.x) {
+  for (int u = first; u < p.units && !failed; u += step) {
     const Unit un = unit_of(p, u);
     for (int64_t rs = un.r0; rs < un.r_end && !failed; rs += kTileRows) {
       // N = the tile's width: a narrower last tile multiplies only its rows
-      const uint32_t idesc =
-          idesc_f16_f32(kQueryRows, static_cast<uint32_t>(tile_width(rs, un.r_end)));
+      const uint32_t idesc = idesc_f16_f32(kPair ? 2 * kQueryRows : kQueryRows,
+                                           static_cast<uint32_t>(tile_width(rs, un.r_end)));
       const uint32_t b = tc & 1u;
       if (!mbar_wait(&sm.acc_empty[b], ((tc >> 1) & 1u) ^ 1u, p.err, kErrTimeoutAccEmpty)) {
         failed = true;
@@ -290,24 +333,32 @@ __device__ void mma_issuer(const ScanParams& p, const Smem& sm, uint32_t tmem_ba
           break;
         }
         tc_fence_after();
-        const uint32_t a0 = smem_addr(sm.stages + static_cast<size_t>(slot) * kStageBytes);
+        const uint32_t a0 = smem_addr(sm.stages + static_cast<size_t>(slot) * sbytes);
         const uint32_t b0 = a0 + kStageA;
 #pragma unroll
         for (int kk = 0; kk < kKChunk / 16; ++kk) {
           // advancing 16 fp16 (32 bytes) inside the 128-byte swizzle atom
-          umma_f16_ss(d_tmem, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32),
-                      idesc, (kc | kk) != 0 ? 1u : 0u);
+          if constexpr (kPair) {
+            umma_f16_ss_pair(d_tmem, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32),
+                             idesc, (kc | kk) != 0 ? 1u : 0u);
+          } else {
+            umma_f16_ss(d_tmem, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32),
+                        idesc, (kc | kk) != 0 ? 1u : 0u);
+          }
         }
-        umma_commit(&sm.empty[slot]);
+        if constexpr (kPair) umma_commit_pair_both(&sm.empty[slot]);
+        else umma_commit(&sm.empty[slot]);
         ++it;
       }
       if (failed) break;
-      umma_commit(&sm.acc_full[b]);
+      if constexpr (kPair) umma_commit_pair_both(&sm.acc_full[b]);
+      else umma_commit(&sm.acc_full[b]);
       ++tc;
     }
   }
   // All MMAs of this thread must be complete before TMEM is released.
-  umma_commit(sm.drain);
+  if constexpr (kPair) umma_commit_pair_own(sm.drain);
+  else umma_commit(sm.drain);
   drain_wait(sm.drain, 0);
 }
 
@@ -469,9 +520,12 @@ __device__ __forceinline__ void flush_buffer(RowState<kReg>& st, const Smem& sm,
 // Survivors of a 16-column group are appended one per lane per round (the
 // lowest remaining column first), so a group costs as many rounds as its
 // busiest lane has survivors, usually one.
-template <int kMetric, bool kReg>
+template <int kMetric, bool kReg, bool kPair>
 __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base, int warp,
                          int lane) {
+  const uint32_t crank = kPair ? cluster_ctarank() : 0u;
+  const int first = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int step = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
   const int quad = warp & 3;              // TMEM lane quadrant this warp may access
   const int row = quad * 32 + lane;       // query row within the unit's block
   const bool warp_active = quad * 32 < p.query_block;
@@ -480,12 +534,13 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
   const float kInf = __int_as_float(0x7f800000);
   uint32_t tc = 0;
   bool failed = false;
-  for (int u = blockIdx.x; u < p.units && !failed; u += gridDim.x) {
+  for (int u = first; u < p.units && !failed; u += step) {
     const Unit un = unit_of(p, u);
     // rows at or past row_lim are masked: the dataset's end, or (in a
     // narrower last tile) accumulator columns the tile's MMAs did not write
     const int64_t row_lim = un.r_end < p.n_rows ? un.r_end : p.n_rows;
-    const int64_t q = static_cast<int64_t>(un.m) * p.query_block + row;
+    const int64_t q = static_cast<int64_t>(un.m) * p.unit_queries +
+                      static_cast<int64_t>(crank) * kQueryRows + row;
     const bool valid_q = warp_active && row < p.query_block && q < p.n_queries;
     const float qn = valid_q ? p.query_norms[q] : 0.0f;
     RowState<kReg> st;
@@ -655,7 +710,11 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
+      if (lane == 0) {
+        // with pairs the first CTA's MMAs wait for both CTAs' epilogues
+        if constexpr (kPair) mbar_arrive_cluster(mapa_shared(&sm.acc_empty[b], 0));
+        else mbar_arrive(&sm.acc_empty[b]);
+      }
       ++tc;
       // survivors enter the heap at every tile end so thr tightens early (the
       // accumulator is already released; this overlaps the next tile's MMAs)
@@ -709,7 +768,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
   }
 }
 
-template <int kMetric, bool kReg>
+template <int kMetric, bool kReg, bool kPair>
 __global__ void __launch_bounds__(kScanThreads, 1)
     knn_scan_kernel(const __grid_constant__ CUtensorMap qmap,
                     const __grid_constant__ CUtensorMap xmap,
@@ -720,13 +779,16 @@ __global__ void __launch_bounds__(kScanThreads, 1)
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
+    // with pairs, the first CTA's full barriers take one arrival from each
+    // CTA's producer and its acc_empty barriers one from each of the eight
+    // epilogue warps (the second CTA's barriers of those kinds go unused)
     for (int s = 0; s < p.stages; ++s) {
-      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.full[s], kPair ? 2 : 1);
       mbar_init(&sm.empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.acc_full[b], 1);
-      mbar_init(&sm.acc_empty[b], 4);
+      mbar_init(&sm.acc_empty[b], kPair ? 8 : 4);
     }
     mbar_init(sm.drain, 1);
     fence_mbar_init();
@@ -737,11 +799,18 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     tma_prefetch_map(&xmap_tail);
   }
   if (warp == 1) {
-    tmem_alloc(sm.tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair(sm.tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(sm.tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // the peer's barriers are initialised before any remote arrival
+  if constexpr (kPair) cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *sm.tmem_slot;
   // Launched as a programmatic dependent: the set-up above overlaps the tail
@@ -753,18 +822,22 @@ __global__ void __launch_bounds__(kScanThreads, 1)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
-    if (lane == 0) producer(&qmap, &xmap, &xmap_tail, p, sm);
+    if (lane == 0) producer<kPair>(&qmap, &xmap, &xmap_tail, p, sm);
   } else if (warp == 1) {
-    if (lane == 0) mma_issuer(p, sm, tmem_base);
+    if (lane == 0 && (!kPair || cluster_ctarank() == 0)) mma_issuer<kPair>(p, sm, tmem_base);
   } else {
-    epilogue<kMetric, kReg>(p, sm, tmem_base, warp, lane);
+    epilogue<kMetric, kReg, kPair>(p, sm, tmem_base, warp, lane);
   }
 
   tc_fence_before();
   __syncthreads();
+  // neither CTA of a pair leaves while the other may still signal its
+  // barriers or the MMAs may still read its shared memory
+  if constexpr (kPair) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if constexpr (kPair) tmem_dealloc_pair(tmem_base, kTmemCols);
+    else tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
@@ -851,6 +924,61 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
   if (num_sms <= 0) num_sms = 148;
   const int64_t heap_per_query = (k + kRowBuf) * 8;  // heap + survivor buffer
   const int64_t budget = kSmemLimit - kSmemReserve;
+  const int64_t row_tiles = (n_rows + kTileRows - 1) / kTileRows;
+  *out = Plan{};
+  out->row_tiles = row_tiles;
+  // Splits of the rows for query_tiles tiles over `slots` concurrent units:
+  // the count minimising waves x (tiles per unit + 1), a unit's narrower
+  // last tile counted by its width, with the partial lists capped at 1 GiB.
+  auto pick_splits = [&](int64_t query_tiles, int64_t n_gran, int64_t gran, int64_t slots) {
+    if (query_tiles == 1) return n_gran < slots ? n_gran : slots;
+    const int64_t max_s = n_gran < 4 * slots ? n_gran : 4 * slots;
+    int64_t best_s = 1;
+    double best = -1.0;
+    for (int64_t s = 1; s <= max_s; ++s) {
+      if (n_queries * s * k * 8 > (int64_t(1) << 30) && s > 1) break;
+      const int64_t units = query_tiles * s;
+      const int64_t waves = (units + slots - 1) / slots;
+      const double per_unit = static_cast<double>((n_gran + s - 1) / s) * gran / kTileRows;
+      const double cost = static_cast<double>(waves) * (per_unit + 1.0);
+      if (best < 0 || cost < best) {
+        best = cost;
+        best_s = s;
+      }
+    }
+    return best_s;
+  };
+  // More than one 128-query tile and heaps so large (k >= 62) that one CTA
+  // would keep fewer than 3 pipeline stages: CTA pairs (M = 256 over two
+  // SMs, each loading half of every dataset tile into stages of 32 KiB
+  // instead of 48).  Measured on one B200: Q = 10,000, K = 100 over 1.25M
+  // rows 32.2 -> 28.7 ms; with 4 stages already (K = 10) pairs were 6%
+  // slower, so smaller k stays on single CTAs.
+  const int64_t pair_stages = (budget - kQueryRows * heap_per_query) / stage_bytes(1);
+  const int64_t single_stages = (budget - kQueryRows * heap_per_query) / kStageBytes;
+  if (n_queries > kQueryRows && single_stages < 3 && pair_stages >= 2 && num_sms >= 2) {
+    const int64_t gran = 2 * kGranRows;
+    const int64_t n_gran = (n_rows + gran - 1) / gran;
+    const int64_t query_tiles = (n_queries + 2 * kQueryRows - 1) / (2 * kQueryRows);
+    const int64_t pairs = num_sms / 2;
+    const int64_t splits = pick_splits(query_tiles, n_gran, gran, pairs);
+    const int64_t units = query_tiles * splits;
+    if (units > INT32_MAX || n_gran * gran > INT32_MAX + int64_t(kTileRows)) return 6;
+    const int64_t stages = pair_stages > kMaxStages ? kMaxStages : pair_stages;
+    out->query_block = kQueryRows;
+    out->query_tiles = query_tiles;
+    out->splits = splits;
+    out->units = units;
+    out->grid = 2 * (units < pairs ? units : pairs);
+    out->stages = stages;
+    out->smem_bytes = kSmemReserve + stages * stage_bytes(1) + kQueryRows * heap_per_query;
+    out->partial_bytes = n_queries * splits * k * 8;
+    out->pair = 1;
+    out->gran_rows = gran;
+    out->unit_queries = 2 * kQueryRows;
+    (void)dim;
+    return 0;
+  }
   int64_t qb_cap = (budget - 2 * kStageBytes) / heap_per_query;
   qb_cap = (qb_cap / 32) * 32;
   if (qb_cap > kQueryRows) qb_cap = kQueryRows;
@@ -861,42 +989,21 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
   if (stages > kMaxStages) stages = kMaxStages;
   if (stages < 2) return 6;
   const int64_t query_tiles = (n_queries + qb - 1) / qb;
-  const int64_t row_tiles = (n_rows + kTileRows - 1) / kTileRows;
   const int64_t n_gran = (n_rows + kGranRows - 1) / kGranRows;
-  int64_t splits;
-  if (query_tiles == 1) {
-    splits = n_gran < num_sms ? n_gran : num_sms;
-  } else {
-    // Pick the split count minimising waves x (tiles per unit + 1), a unit's
-    // narrower last tile counted by its width, with the partial lists capped
-    // at 1 GiB.
-    const int64_t max_s = n_gran < 4 * num_sms ? n_gran : 4 * num_sms;
-    splits = 1;
-    double best = -1.0;
-    for (int64_t s = 1; s <= max_s; ++s) {
-      if (n_queries * s * k * 8 > (int64_t(1) << 30) && s > 1) break;
-      const int64_t units = query_tiles * s;
-      const int64_t waves = (units + num_sms - 1) / num_sms;
-      const double per_unit =
-          static_cast<double>((n_gran + s - 1) / s) * kGranRows / kTileRows;
-      const double cost = static_cast<double>(waves) * (per_unit + 1.0);
-      if (best < 0 || cost < best) {
-        best = cost;
-        splits = s;
-      }
-    }
-  }
+  const int64_t splits = pick_splits(query_tiles, n_gran, kGranRows, num_sms);
   const int64_t units = query_tiles * splits;
   if (units > INT32_MAX || n_gran * kGranRows > INT32_MAX + int64_t(kTileRows)) return 6;
   out->query_block = qb;
   out->query_tiles = query_tiles;
-  out->row_tiles = row_tiles;
   out->splits = splits;
   out->units = units;
   out->grid = units < num_sms ? units : num_sms;
   out->stages = stages;
   out->smem_bytes = kSmemReserve + stages * kStageBytes + qb * heap_per_query;
   out->partial_bytes = n_queries * splits * k * 8;
+  out->pair = 0;
+  out->gran_rows = kGranRows;
+  out->unit_queries = qb;
   (void)dim;
   return 0;
 }
@@ -912,11 +1019,15 @@ cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
   if (p.metric != KNN_METRIC_L2_EXPANDED && p.metric != KNN_METRIC_INNER_PRODUCT)
     return cudaErrorInvalidValue;
   const bool ip = p.metric == KNN_METRIC_INNER_PRODUCT;
+#define KNN_SCAN_FNS(M)                                                          \
+  reinterpret_cast<const void*>(knn_scan_kernel<M, false, false>),              \
+      reinterpret_cast<const void*>(knn_scan_kernel<M, true, false>),           \
+      reinterpret_cast<const void*>(knn_scan_kernel<M, false, true>),           \
+      reinterpret_cast<const void*>(knn_scan_kernel<M, true, true>)
+  static const void* const fns[8] = {KNN_SCAN_FNS(KNN_METRIC_L2_EXPANDED),
+                                     KNN_SCAN_FNS(KNN_METRIC_INNER_PRODUCT)};
+#undef KNN_SCAN_FNS
   if (dev < 0 || dev >= 64 || !configured[dev]) {
-    const void* fns[] = {reinterpret_cast<const void*>(knn_scan_kernel<KNN_METRIC_L2_EXPANDED, false>),
-                         reinterpret_cast<const void*>(knn_scan_kernel<KNN_METRIC_L2_EXPANDED, true>),
-                         reinterpret_cast<const void*>(knn_scan_kernel<KNN_METRIC_INNER_PRODUCT, false>),
-                         reinterpret_cast<const void*>(knn_scan_kernel<KNN_METRIC_INNER_PRODUCT, true>)};
     for (const void* fn : fns) {
       e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(kSmemLimit));
@@ -924,30 +1035,31 @@ cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
     }
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
+  if (p.n_gran != (p.n_rows + p.gran_rows - 1) / p.gran_rows || p.splits < 1 ||
+      p.splits > p.n_gran || (p.pair != 0) != (plan.pair != 0) ||
+      (p.pair && (plan.grid % 2 != 0 || p.gran_rows != 2 * kGranRows ||
+                  p.unit_queries != 2 * kQueryRows || p.query_block != kQueryRows)))
+    return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(plan.grid));
   cfg.blockDim = dim3(kScanThreads);
   cfg.dynamicSmemBytes = static_cast<size_t>(plan.smem_bytes);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = overlap ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = p.pair ? 2 : 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (p.n_gran != (p.n_rows + kGranRows - 1) / kGranRows || p.splits < 1 ||
-      p.splits > p.n_gran)
-    return cudaErrorInvalidValue;
+  cfg.numAttrs = p.pair ? 2 : 1;
   // small k: the register top-k (the pilot pass only runs for k > kRegK)
   const bool reg = p.k <= kRegK && !p.pilot;
-  if (ip)
-    return reg ? cudaLaunchKernelEx(&cfg, knn_scan_kernel<KNN_METRIC_INNER_PRODUCT, true>, qmap,
-                                    xmap, xmap_tail, p)
-               : cudaLaunchKernelEx(&cfg, knn_scan_kernel<KNN_METRIC_INNER_PRODUCT, false>, qmap,
-                                    xmap, xmap_tail, p);
-  return reg ? cudaLaunchKernelEx(&cfg, knn_scan_kernel<KNN_METRIC_L2_EXPANDED, true>, qmap, xmap,
-                                  xmap_tail, p)
-             : cudaLaunchKernelEx(&cfg, knn_scan_kernel<KNN_METRIC_L2_EXPANDED, false>, qmap, xmap,
-                                  xmap_tail, p);
+  const void* fn = fns[(ip ? 4 : 0) + (p.pair ? 2 : 0) + (reg ? 1 : 0)];
+  void* args[] = {const_cast<CUtensorMap*>(&qmap), const_cast<CUtensorMap*>(&xmap),
+                  const_cast<CUtensorMap*>(&xmap_tail), const_cast<ScanParams*>(&p)};
+  return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 }  // namespace knn

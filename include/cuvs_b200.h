@@ -80,7 +80,7 @@ typedef struct knn_index knn_index;
  * reference, exposed for tests and tooling). */
 typedef struct knn_plan {
   int64_t query_block;   /* queries per CTA work unit (multiple of 32) */
-  int64_t query_tiles;   /* ceil(n_queries / query_block) */
+  int64_t query_tiles;   /* ceil(n_queries / unit_queries) */
   int64_t row_tiles;     /* ceil(n_rows / 256) */
   int64_t splits;        /* row-range splits per query tile */
   int64_t units;         /* query_tiles * splits */
@@ -88,6 +88,8 @@ typedef struct knn_plan {
   int64_t stages;        /* shared-memory pipeline stages */
   int64_t smem_bytes;    /* dynamic shared memory per CTA */
   int64_t partial_bytes; /* scratch for per-unit top-k lists */
+  int64_t pair;          /* 1: pairs of CTAs share each dataset tile (cta_group::2) */
+  int64_t unit_queries;  /* queries per work unit (query_block, or 256 with pairs) */
 } knn_plan;
 
 /* Human-readable text for the calling thread's last failure. */

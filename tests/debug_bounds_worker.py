@@ -8,7 +8,8 @@ bounds.  The shapes cover what the kernels index differently: dimensions
 below, at and above the 64-wide slice and not multiples of 8, datasets
 smaller than one granule, ragged last tiles, k above the row count
 (padding), the register top-k (k <= 16), the heap (k > 16) with the pilot
-pass (k >= 17), several query tiles, the inner product, exact re-ranking,
+pass (k >= 17), several query tiles, CTA pairs (more than 128 queries with
+k >= 62), the inner product, exact re-ranking,
 the search without allocation, host and device buffers and graph replay.
 Results are checked against the oracle too.  Exit code 0 = pass.
 Run in its own process: the binding loads one engine library per process.
@@ -38,6 +39,7 @@ def main():
         (5, 3, 2, 8, 0), (31, 64, 3, 10, 0), (257, 65, 7, 16, 0), (1000, 72, 33, 17, 0),
         (4097, 128, 130, 32, 0), (20011, 100, 37, 100, 0), (3000, 200, 300, 10, 0),
         (600, 96, 5, 256, 0), (9000, 64, 64, 10, 1), (777, 130, 9, 50, 1),
+        (20011, 72, 257, 64, 0), (3001, 200, 600, 100, 1),  # CTA pairs
     ]
     for n, dim, nq, k, metric in cases:
         base = rng.standard_normal((n, dim), dtype=np.float32)

@@ -60,7 +60,11 @@ def test_planner_fits_shared_memory(engine, nq, k):
     assert p["smem_bytes"] <= 232448
     assert p["stages"] >= 2
     assert p["query_block"] % 32 == 0 and 32 <= p["query_block"] <= 128
-    assert p["query_tiles"] * p["query_block"] >= nq
+    assert p["query_tiles"] * p["unit_queries"] >= nq
+    # CTA pairs only where one CTA would keep fewer than 3 stages (k >= 62)
+    assert p["pair"] == (1 if nq > 128 and k >= 62 else 0), p
+    if p["pair"]:
+        assert p["grid"] % 2 == 0 and p["unit_queries"] == 256 and p["query_block"] == 128
     assert p["units"] == p["query_tiles"] * p["splits"]
     assert 1 <= p["splits"] <= p["row_tiles"]
     assert p["grid"] == min(p["units"], 148)

@@ -88,6 +88,7 @@ SHAPES = [
     (5000, 1024, 129, 10),
     (4099, 256, 16, 256),
     (700, 64, 300, 100),
+    (20011, 72, 257, 64),
 ]
 
 

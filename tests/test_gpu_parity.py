@@ -126,6 +126,11 @@ SHAPES = [
     (2500, 128, 100, 256),
     (1500, 64, 40, 200),
     (700, 64, 300, 100),
+    # CTA pairs (more than 128 queries, k >= 62): a last pair tile with one
+    # query, a dataset of three 64-row granules, several pair tiles
+    (20011, 72, 257, 64),
+    (130, 33, 129, 62),
+    (3001, 200, 600, 128),
 ]
 
 
