@@ -249,7 +249,11 @@ def cpu_reference_qps(base16_host, q16_host, k, sample_q, threads):
     import oracle
 
     q = q16_host[:sample_q]
-    use_ref = oracle.ref_available()
+    # the reference's build copies the dataset into its index on every call
+    # (one call per thread): past 64 GB of copies the C restatement, which
+    # reads the rows in place, stands in (same results, pinned bit for bit)
+    use_ref = oracle.ref_available() and \
+        base16_host.nbytes * min(threads, sample_q) <= 64 * 10 ** 9
     t0 = time.perf_counter()
     if use_ref:
         idx, dist = oracle.ref_knn(base16_host, q, k, threads=threads)

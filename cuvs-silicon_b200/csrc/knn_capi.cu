@@ -655,9 +655,10 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
                                h->err_dev, l_len));
     launches += 1;
   } else if (uses_peer_exchange(h, nq, k)) {
-    // peer exchange: the local merge writes every query's list into every
-    // rank's exchange buffer over NVLink as epoch-tagged words; the final
-    // merge collects them from its own buffer (bounded wait) and merges
+    // peer exchange, one kernel: each query's block merges this rank's lists,
+    // writes the result into every rank's exchange buffer over NVLink as
+    // epoch-tagged words, collects every rank's list for the query from its
+    // own buffer (bounded wait) and merges them
     knn::Exchange ex = {};
     for (int r = 0; r < h->n_ranks; ++r) ex.base[r] = h->xpeer[r];
     ex.cap_qk = h->xcap;
@@ -668,16 +669,11 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
     ex.err = h->err_dev;
     ex.in_len = l_len;
     ex.mode = 1;
-    KNN_CUDA(knn::launch_merge(ld, li, l_stride, q_stride, n_lists, static_cast<int>(k), nq, off,
-                               nullptr, nullptr, false, h->stream, overlap, &ex));
-    ex.mode = 2;
-    ex.in_len = static_cast<int64_t>(qk) * h->n_ranks;
     ex.dec_d = h->xdec.as<float>();
     ex.dec_i = reinterpret_cast<uint32_t*>(ex.dec_d + qk * h->n_ranks);
-    KNN_CUDA(knn::launch_merge(ex.dec_d, ex.dec_i, k, static_cast<int64_t>(h->n_ranks) * k,
-                               h->n_ranks, static_cast<int>(k), nq, 0, dst_d, dst_i, out_i64,
-                               h->stream, overlap, &ex, neg));
-    launches += 2;
+    KNN_CUDA(knn::launch_merge(ld, li, l_stride, q_stride, n_lists, static_cast<int>(k), nq, off,
+                               dst_d, dst_i, out_i64, h->stream, overlap, &ex, neg));
+    launches += 1;
   } else {
     // local merge into the send buffer: [dist k floats | idx k uint32] per query
     const size_t list_bytes = qk * 8;

@@ -149,11 +149,11 @@ struct Exchange {
   int64_t cap_qk;
   int n_ranks;
   int rank;
-  int mode;               // 0 none; 1 push this rank's lists to every rank; 2 receive and merge
+  int mode;               // 0 none; 1 exchange (push, receive every rank's list, merge)
   const uint32_t* epoch;  // device word: the current search's epoch (>= 1)
-  uint64_t wait_ns;       // mode 2: how long to wait for a peer's list
+  uint64_t wait_ns;       // how long to wait for a peer's list
   int* err;               // device error word (wait timeouts, debug bounds checks)
-  float* dec_d;           // mode 2: received lists, decoded: [q][n_ranks][k]
+  float* dec_d;           // received lists, decoded: [q][n_ranks][k]
   uint32_t* dec_i;
   int64_t in_len;         // entries of the merge's in_d / in_i (debug bounds checks)
 };
@@ -168,14 +168,13 @@ inline int64_t exchange_words(int n_ranks, int64_t cap_qk) {
 // List l of query q starts at in_{d,i}[q * stride_query + l * stride_list].
 // Valid indices get index_offset added.  out_i is uint32 (no-neighbour =
 // UINT32_MAX) or int64 (no-neighbour = -1) per out_i64.
-// `ex` (optional) selects the peer exchange: mode 1 writes each query's
-// result into every rank's exchange buffer instead of out_d/out_i; mode 2
-// receives every rank's list for the query from this rank's buffer (bounded
-// wait), decodes them to ex->dec_d/dec_i (which in_d/in_i must name, with
-// stride_list = k and stride_query = n_ranks * k) and merges them.
-// `negate_out` writes -d to out_d (the inner-product metric orders by -q.x
-// internally and reports q.x; padding becomes -inf).  Lists written to an
-// exchange buffer (mode 1) are never negated.
+// `ex` (optional, mode 1) selects the peer exchange: the block of query q
+// merges this rank's lists, writes the result into every rank's exchange
+// buffer, then receives every rank's list for q from this rank's buffer
+// (bounded wait), decodes them to ex->dec_d/dec_i and merges those into
+// out_d/out_i.  `negate_out` writes -d to out_d (the inner-product metric
+// orders by -q.x internally and reports q.x; padding becomes -inf); lists
+// written to an exchange buffer are never negated.
 // err, in_len (optional): the device error word and the number of entries
 // of in_d / in_i, for the debug build's bounds checks (with an exchange,
 // ex->err and ex->in_len are used instead).

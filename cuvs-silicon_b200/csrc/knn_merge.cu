@@ -335,11 +335,11 @@ __device__ bool receive_lists(const Exchange& ex, uint32_t epoch, int64_t q, int
 // rest padding) to the output, or in mode 1 to every rank's exchange buffer
 // as epoch-tagged words.  Called by every thread of the block.
 template <typename OutIdx>
-__device__ void emit_result(const Exchange& ex, uint32_t epoch, int64_t q, int k,
+__device__ void emit_result(const Exchange& ex, bool push, uint32_t epoch, int64_t q, int k,
                             const float* rd, const uint32_t* ri, int count,
                             int64_t index_offset, float* out_d, OutIdx* out_i, float sign) {
   const float kInf = __int_as_float(0x7f800000);
-  if (ex.mode != 1) {
+  if (!push) {
     for (int e = threadIdx.x; e < k; e += blockDim.x) {
       const bool have = e < count;
       store_out(out_d, out_i, q * k + e, have ? rd[e] : kInf, have ? ri[e] : kNoIndex,
@@ -369,7 +369,7 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
                                             int n_lists, int k, int64_t index_offset,
                                             float* __restrict__ out_d,
                                             OutIdx* __restrict__ out_i, const Exchange& ex,
-                                            uint32_t epoch, float sign) {
+                                            bool push, uint32_t epoch, float sign) {
   extern __shared__ uint8_t smem_raw[];
   float* sd = reinterpret_cast<float*>(smem_raw);
   uint32_t* si = reinterpret_cast<uint32_t*>(sd + kStageEntries);
@@ -392,7 +392,7 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
   if (n_lists > kSelCap) {
     fold_merge<E>(sd, si, qd, qi, stride_list, n_lists, k, sd + kSelCap, si + kSelCap);
     __syncthreads();
-    emit_result(ex, epoch, q, k, sd + kSelCap, si + kSelCap, k, index_offset, out_d, out_i, sign);
+    emit_result(ex, push, epoch, q, k, sd + kSelCap, si + kSelCap, k, index_offset, out_d, out_i, sign);
     return;
   }
   int p2 = 1;
@@ -564,14 +564,14 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
     __syncthreads();
     fold_merge<E>(sd, si, qd, qi, stride_list, n_lists, k, cd, ci);
     __syncthreads();
-    emit_result(ex, epoch, q, k, cd, ci, k, index_offset, out_d, out_i, sign);
+    emit_result(ex, push, epoch, q, k, cd, ci, k, index_offset, out_d, out_i, sign);
     return;
   }
   if (count <= (k > kLongList ? kRankPlaceLong : kRankPlaceMax)) {
     // candidates are distinct (distinct row indices): rank counting places
     // the first k of them, sorted, in front of the selection array
     rank_place(cd, ci, count, seld, seli, k);
-    emit_result(ex, epoch, q, k, seld, seli, count, index_offset, out_d, out_i, sign);
+    emit_result(ex, push, epoch, q, k, seld, seli, count, index_offset, out_d, out_i, sign);
     return;
   }
   int c2 = 1;
@@ -582,7 +582,7 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
   }
   __syncthreads();
   block_sort(cd, ci, c2);
-  emit_result(ex, epoch, q, k, cd, ci, count, index_offset, out_d, out_i, sign);
+  emit_result(ex, push, epoch, q, k, cd, ci, count, index_offset, out_d, out_i, sign);
 }
 
 template <int E, typename OutIdx>
@@ -598,8 +598,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
   const int64_t q = blockIdx.x;
   // Everything this kernel reads was written by kernels before it in the
   // stream; in particular the exchange epoch, which the query conversion
-  // that opened this search incremented.  Mode 2 waits for the local merge
-  // (mode 1) of this rank too, whose stores carry this rank's own list.
+  // that opened this search incremented.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // debug builds: every list this block reads (and, with an exchange, every
   // slot it writes or polls) lies inside its buffer
@@ -608,14 +607,22 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
   if (ex.mode != 0 && !in_bounds((q + 1) * k <= ex.cap_qk && ex.n_ranks <= kMaxRanks, ex.err))
     return;
   const uint32_t epoch = ex.mode != 0 ? *reinterpret_cast<const volatile uint32_t*>(ex.epoch) : 0u;
-  if (ex.mode == 2) {
+  if (ex.mode == 1) {
+    // Exchange, one block per query from end to end: merge this rank's
+    // per-unit lists and push the result into every rank's exchange buffer
+    // (NVLink stores), then collect every rank's list for the same query
+    // from this rank's own buffer (bounded wait), decode and merge them.
+    // No block waits for another block of this GPU, only for the block of
+    // the same query on each peer.
+    merge_query<E, OutIdx>(in_d, in_i, stride_list, stride_query, n_lists, k, index_offset,
+                           nullptr, nullptr, ex, true, epoch, 1.0f);
     if (receive_lists(ex, epoch, q, k, &s_abort))
-      merge_query<E, OutIdx>(in_d, in_i, stride_list, stride_query, n_lists, k, index_offset,
-                             out_d, out_i, ex, epoch, sign);
+      merge_query<E, OutIdx>(ex.dec_d, ex.dec_i, k, static_cast<int64_t>(ex.n_ranks) * k,
+                             ex.n_ranks, k, 0, out_d, out_i, ex, false, epoch, sign);
     return;
   }
   merge_query<E, OutIdx>(in_d, in_i, stride_list, stride_query, n_lists, k, index_offset, out_d,
-                         out_i, ex, epoch, sign);
+                         out_i, ex, false, epoch, sign);
 }
 
 template <int E>
