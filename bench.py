@@ -61,7 +61,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--n", type=int, default=1_000_000)
+    # --rows is the same option: under torch.distributed.run "--n" is an
+    # ambiguous prefix of the launcher's own options
+    ap.add_argument("--n", "--rows", dest="n", type=int, default=1_000_000)
     ap.add_argument("--dim", type=int, default=1024)
     ap.add_argument("--q", type=int, default=100)
     ap.add_argument("--k", type=int, default=10)
@@ -129,18 +131,24 @@ def roofline(n_shard, dim, nq, kernel_ms):
 
 
 def profile_traffic(a, n_shard):
-    """dram bytes per scan launch from the committed ncu figure
+    """dram bytes per scan launch from the committed ncu figures
     (profiles/knn_scan_traffic.json: dram__bytes_read.sum +
-    dram__bytes_write.sum of one captured launch), scaled to this shard's rows
-    when it was captured on a different row count (the scan's traffic grows
-    in proportion to the rows it reads)."""
+    dram__bytes_write.sum of one captured launch per configuration), scaled
+    to this shard's rows when captured on a different row count (the scan's
+    traffic grows in proportion to the rows it reads).  Uses the capture of
+    the same dim and k whose query count is within a factor of two of this
+    run's; None when there is none."""
     path = os.path.join(ROOT, "profiles", "knn_scan_traffic.json")
     try:
         with open(path) as f:
             v = json.load(f)
-        if int(v["captured_dim"]) != a.dim or int(v["captured_queries"]) < a.q // 2:
-            return None
-        return float(v["traffic_bytes_per_launch"]) * n_shard / float(v["captured_rows"])
+        for c in v["captures"]:
+            if int(c["captured_dim"]) != a.dim or int(c["captured_k"]) != a.k:
+                continue
+            cq = int(c["captured_queries"])
+            if a.q // 2 <= cq <= 2 * a.q:
+                return float(c["traffic_bytes_per_launch"]) * n_shard / float(c["captured_rows"])
+        return None
     except Exception:
         return None
 

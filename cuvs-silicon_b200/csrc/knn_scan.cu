@@ -637,8 +637,15 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
               // query's k-th distance over the shard: share it now
               const uint32_t bits = dist_order_bits(tk);
               if (p.bound && bits < st.pub && in_bounds(q < p.n_queries, p.err)) {
-                atomicMin(p.bound + q, bits);
+                // publish ours and take back the smallest bound published so
+                // far: the units seed at about the same time, so the minimum
+                // over those that already have is far tighter than our own
+                const uint32_t seen = atomicMin(p.bound + q, bits);
                 st.pub = bits;
+                if (seen < bits) {
+                  const float bnd = dist_from_order_bits(seen);
+                  if (bnd < kInf) st.thr = fminf(st.thr, next_up(bnd));
+                }
               }
             }
           }

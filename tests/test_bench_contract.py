@@ -35,3 +35,24 @@ def test_reference_arm_prints_one_contract_line():
     assert cfg["metric"] == "L2Expanded" and cfg["exact_fp32_rerank"] is False
     assert line["cpu_baseline"]["kind"] in ("reference", "port")
     assert line["cpu_baseline"]["cores"] >= 1
+
+
+def test_roofline_traffic_comes_from_the_matching_capture():
+    # the committed ncu figures are per (dim, k, query count) and scale with
+    # the rows a launch scans; a configuration without a capture reports None
+    import types
+
+    sys.path.insert(0, ROOT)
+    import bench
+
+    with open(os.path.join(ROOT, "profiles", "knn_scan_traffic.json")) as f:
+        caps = json.load(f)["captures"]
+    for c in caps:
+        a = types.SimpleNamespace(dim=c["captured_dim"], k=c["captured_k"],
+                                  q=c["captured_queries"])
+        assert c["traffic_bytes_per_launch"] == c["dram_bytes_read"] + c["dram_bytes_write"]
+        t = bench.profile_traffic(a, 5 * c["captured_rows"])
+        assert t == 5 * c["traffic_bytes_per_launch"]
+        # every row is read about once: traffic within 3% of the fp16 rows
+        assert abs(c["dram_bytes_read"] / (2 * c["captured_rows"] * c["captured_dim"]) - 1) < 0.03
+    assert bench.profile_traffic(types.SimpleNamespace(dim=96, k=10, q=100), 1000) is None
