@@ -570,6 +570,7 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
   p.n_gran = (h->n + plan.gran_rows - 1) / plan.gran_rows;
   p.q_rows = nq_pad;
   p.pair = static_cast<int32_t>(plan.pair);
+  p.compact = static_cast<int32_t>(plan.compact);
   p.gran_rows = static_cast<int32_t>(plan.gran_rows);
   p.unit_queries = static_cast<int32_t>(plan.unit_queries);
   p.ld = h->ld;
@@ -1528,6 +1529,7 @@ int knn_plan_search(int64_t n_rows, int64_t dim, int64_t nq, int64_t k, int num_
   out->partial_bytes = p.partial_bytes;
   out->pair = p.pair;
   out->unit_queries = p.unit_queries;
+  out->compact_heap = p.compact;
   return KNN_OK;
 }
 
@@ -1787,6 +1789,7 @@ int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
   p.n_gran = (h->n + plan.gran_rows - 1) / plan.gran_rows;
   p.q_rows = nq_pad;
   p.pair = static_cast<int32_t>(plan.pair);
+  p.compact = static_cast<int32_t>(plan.compact);
   p.gran_rows = static_cast<int32_t>(plan.gran_rows);
   p.unit_queries = static_cast<int32_t>(plan.unit_queries);
   p.ld = h->ld;

@@ -27,6 +27,7 @@ constexpr int kSmemLimit = 232448;        // sm_100 opt-in dynamic smem per CTA
 constexpr int kSmemReserve = 1024 + 4096 + 512;  // alignment slack + norm staging + barriers
 constexpr int kMaxK = 256;
 constexpr int kRowBuf = 16;       // buffered survivors per query row
+constexpr int64_t kCompactMaxRows = 65535;  // rows of a unit with compact heaps
 constexpr uint32_t kNoIndex = 0xFFFFFFFFu;
 
 // Device-side error codes (written to a kernel's error word; 0 = ok).
@@ -52,6 +53,11 @@ struct ScanParams {
   // (cta_group::2 MMAs, M = 256); a unit then covers 256 query rows, 128
   // per CTA.  Work units split the rows in granules of gran_rows.
   int32_t pair;
+  // Compact heaps (compact = 1, k > 16 only): a heap entry is the distance's
+  // order image (32 bits) and the row's offset from the unit's first row
+  // (16 bits), 6 bytes instead of 8; needs units of at most kCompactMaxRows
+  // rows.
+  int32_t compact;
   int32_t gran_rows;     // kGranRows, or 2 * kGranRows with pairs
   int32_t unit_queries;  // query rows of a unit: query_block, or 256 with pairs
   int32_t k;
@@ -87,6 +93,7 @@ struct Plan {
   int64_t query_block, query_tiles, row_tiles, splits, units, grid, stages;
   int64_t smem_bytes, partial_bytes;
   int64_t pair = 0, gran_rows = kGranRows, unit_queries = 0;
+  int64_t compact = 0;
 };
 
 // Returns 0 and fills `out`, or a KNN_E* status (KNN_EUNSUPPORTED when k is

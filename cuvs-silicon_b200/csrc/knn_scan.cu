@@ -79,47 +79,76 @@ __host__ __device__ constexpr uint64_t empty_key() {
          0xFFFFFFFFull;
 }
 
+// Heap storage.  Full keys (64 bits), or compact entries: the distance's
+// order image in a 32-bit word and the row's offset from the unit's first
+// row in a 16-bit word, 6 bytes an entry (a unit then spans at most
+// kCompactMaxRows rows).  A compact entry reads back as the 64-bit key
+// (image << 32 | offset), which orders like the full key of the same row
+// because every row of the unit has the same first row.
+template <bool kC>
+struct HeapStore {
+  uint64_t* h;
+  __device__ __forceinline__ uint64_t get(int i) const { return h[i]; }
+  __device__ __forceinline__ void set(int i, uint64_t v) const { h[i] = v; }
+};
+template <>
+struct HeapStore<true> {
+  uint32_t* hi;
+  uint16_t* lo;
+  __device__ __forceinline__ uint64_t get(int i) const {
+    return (static_cast<uint64_t>(hi[i]) << 32) | lo[i];
+  }
+  __device__ __forceinline__ void set(int i, uint64_t v) const {
+    hi[i] = static_cast<uint32_t>(v >> 32);
+    lo[i] = static_cast<uint16_t>(v);
+  }
+};
+
 // Max-heap of keys stored column-wise: entry `pos` of query row `row` lives
 // at [pos * stride + row], so the 32 threads of a warp always touch 32
-// consecutive 8-byte words whatever positions they visit.
-__device__ __forceinline__ void heap_sift_down(uint64_t* h, int size, int stride, int row, int pos,
+// consecutive words whatever positions they visit.
+template <typename H>
+__device__ __forceinline__ void heap_sift_down(const H& h, int size, int stride, int row, int pos,
                                                uint64_t key, int cap, int* err) {
   if (!in_bounds(size <= cap && pos < cap && row < stride, err)) return;
   while (true) {
     int c = 2 * pos + 1;
     if (c >= size) break;
-    uint64_t ck = h[c * stride + row];
+    uint64_t ck = h.get(c * stride + row);
     if (c + 1 < size) {
-      const uint64_t rk = h[(c + 1) * stride + row];
+      const uint64_t rk = h.get((c + 1) * stride + row);
       if (rk > ck) {
         c += 1;
         ck = rk;
       }
     }
     if (ck <= key) break;
-    h[pos * stride + row] = ck;
+    h.set(pos * stride + row, ck);
     pos = c;
   }
-  h[pos * stride + row] = key;
+  h.set(pos * stride + row, key);
 }
 
 // Adds `key` at position pos (= the heap's current size) of a max-heap.
-__device__ __forceinline__ void heap_sift_up(uint64_t* h, int stride, int row, int pos,
+template <typename H>
+__device__ __forceinline__ void heap_sift_up(const H& h, int stride, int row, int pos,
                                              uint64_t key, int cap, int* err) {
   if (!in_bounds(pos < cap && row < stride, err)) return;
   while (pos > 0) {
     const int parent = (pos - 1) >> 1;
-    const uint64_t pk = h[parent * stride + row];
+    const uint64_t pk = h.get(parent * stride + row);
     if (pk >= key) break;
-    h[pos * stride + row] = pk;
+    h.set(pos * stride + row, pk);
     pos = parent;
   }
-  h[pos * stride + row] = key;
+  h.set(pos * stride + row, key);
 }
 
 struct Smem {
   uint8_t* stages;
-  uint64_t* heap;  // [k][query_block] keys
+  uint64_t* heap;  // [k][query_block] keys (full keys)
+  uint32_t* heap_hi;  // [k][query_block] distance images (compact heaps)
+  uint16_t* heap_lo;  // [k][query_block] row offsets in the unit (compact heaps)
   uint64_t* buf;   // [kRowBuf][query_block] buffered survivor keys
   float* norm_stage;  // [4 epilogue warps][kAccCols] row norms of the current tile
   uint64_t* full;
@@ -141,9 +170,13 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, const ScanParams& p) {
   const uint32_t base = smem_addr(raw);
   const uint32_t pad = (1024u - (base & 1023u)) & 1023u;
   s.stages = raw + pad;
-  s.heap = reinterpret_cast<uint64_t*>(s.stages +
-                                       static_cast<size_t>(p.stages) * stage_bytes(p.pair));
-  s.buf = s.heap + static_cast<size_t>(p.k) * p.query_block;
+  uint8_t* const heap0 = s.stages + static_cast<size_t>(p.stages) * stage_bytes(p.pair);
+  const size_t entries = static_cast<size_t>(p.k) * p.query_block;
+  s.heap = reinterpret_cast<uint64_t*>(heap0);
+  s.heap_hi = reinterpret_cast<uint32_t*>(heap0);
+  s.heap_lo = reinterpret_cast<uint16_t*>(s.heap_hi + entries);
+  // query_block is a multiple of 32, so the compact arrays end 8-byte aligned
+  s.buf = p.compact ? reinterpret_cast<uint64_t*>(s.heap_lo + entries) : s.heap + entries;
   s.norm_stage = reinterpret_cast<float*>(s.buf + static_cast<size_t>(kRowBuf) * p.query_block);
   uintptr_t b = reinterpret_cast<uintptr_t>(s.norm_stage + 4 * kAccCols);
   b = (b + 7) & ~static_cast<uintptr_t>(7);
@@ -460,9 +493,17 @@ __device__ __forceinline__ void topk_insert(uint64_t (&a)[kRegK], uint64_t x) {
 // lanes run the same number of iterations (the warp's largest buffer), so
 // the updates of the 32 query rows proceed in lock-step.  Heap path: the
 // heap grows by sift-up until it holds k entries, then replaces its root.
-template <int kMetric, bool kReg>
+// Compact heaps (kC) hold keys relative to the unit's first row `base`:
+// a buffered key's index is rebased before it is compared or stored.
+template <bool kC>
+__device__ __forceinline__ HeapStore<kC> heap_of(const Smem& sm) {
+  if constexpr (kC) return HeapStore<true>{sm.heap_hi, sm.heap_lo};
+  else return HeapStore<false>{sm.heap};
+}
+
+template <int kMetric, bool kReg, bool kC>
 __device__ __forceinline__ void flush_buffer(RowState<kReg>& st, const Smem& sm, int k,
-                                             int stride, int row, int* err) {
+                                             int stride, int row, uint32_t base, int* err) {
   const int maxc = __reduce_max_sync(0xffffffffu, st.cnt);
   if (!in_bounds(maxc <= kRowBuf, err)) return;
   if constexpr (kReg) {
@@ -474,15 +515,18 @@ __device__ __forceinline__ void flush_buffer(RowState<kReg>& st, const Smem& sm,
     }
     st.root = st.top[kRegK - 1];
   } else {
+    const HeapStore<kC> heap = heap_of<kC>(sm);
     for (int b = 0; b < maxc; ++b) {
       if (b < st.cnt) {
-        const uint64_t key = sm.buf[b * stride + row];
+        uint64_t key = sm.buf[b * stride + row];
+        if constexpr (kC)
+          key = (key & 0xFFFFFFFF00000000ull) | (static_cast<uint32_t>(key) - base);
         if (st.size < k) {
-          heap_sift_up(sm.heap, stride, row, st.size, key, k, err);
-          if (++st.size == k) st.root = sm.heap[row];
+          heap_sift_up(heap, stride, row, st.size, key, k, err);
+          if (++st.size == k) st.root = heap.get(row);
         } else if (key < st.root) {
-          heap_sift_down(sm.heap, k, stride, row, 0, key, k, err);
-          st.root = sm.heap[row];
+          heap_sift_down(heap, k, stride, row, 0, key, k, err);
+          st.root = heap.get(row);
         }
       }
     }
@@ -520,7 +564,7 @@ __device__ __forceinline__ void flush_buffer(RowState<kReg>& st, const Smem& sm,
 // Survivors of a 16-column group are appended one per lane per round (the
 // lowest remaining column first), so a group costs as many rounds as its
 // busiest lane has survivors, usually one.
-template <int kMetric, bool kReg, bool kPair>
+template <int kMetric, bool kReg, bool kC, bool kPair>
 __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base, int warp,
                          int lane) {
   const uint32_t crank = kPair ? cluster_ctarank() : 0u;
@@ -536,6 +580,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
   bool failed = false;
   for (int u = first; u < p.units && !failed; u += step) {
     const Unit un = unit_of(p, u);
+    const uint32_t base = static_cast<uint32_t>(un.r0);  // compact heaps' offsets start here
     // rows at or past row_lim are masked: the dataset's end, or (in a
     // narrower last tile) accumulator columns the tile's MMAs did not write
     const int64_t row_lim = un.r_end < p.n_rows ? un.r_end : p.n_rows;
@@ -670,7 +715,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
             for (int j = 0; j < kRowBuf; ++j) mask |= (dv[h + j] < st.thr ? 1u : 0u) << j;
             if (__any_sync(0xffffffffu, mask != 0)) {
               if (__any_sync(0xffffffffu, st.cnt + __popc(mask) > kRowBuf)) {
-                flush_buffer<kMetric, kReg>(st, sm, k, stride, row, p.err);
+                flush_buffer<kMetric, kReg, kC>(st, sm, k, stride, row, base, p.err);
                 mask = 0;
 #pragma unroll
                 for (int j = 0; j < kRowBuf; ++j) mask |= (dv[h + j] < st.thr ? 1u : 0u) << j;
@@ -726,7 +771,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
       // survivors enter the heap at every tile end so thr tightens early (the
       // accumulator is already released; this overlaps the next tile's MMAs)
       if (warp_active && __any_sync(0xffffffffu, st.cnt > 0)) {
-        flush_buffer<kMetric, kReg>(st, sm, k, stride, row, p.err);
+        flush_buffer<kMetric, kReg, kC>(st, sm, k, stride, row, base, p.err);
         if (p.bound && valid_q && st.root != empty_key<kMetric>()) {
           const uint32_t bits = dist_order_bits(key_dist<kMetric>(st.root));
           if (bits < st.pub && in_bounds(q < p.n_queries, p.err)) {
@@ -738,7 +783,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
     }
     if (failed) break;
     if (p.pilot) continue;
-    if (warp_active) flush_buffer<kMetric, kReg>(st, sm, k, stride, row, p.err);
+    if (warp_active) flush_buffer<kMetric, kReg, kC>(st, sm, k, stride, row, base, p.err);
     const bool out_ok = !valid_q || in_bounds(q < p.n_queries && u / p.query_tiles < p.splits,
                                               p.err);
     if (kReg && valid_q && out_ok) {
@@ -756,26 +801,27 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
     } else if (valid_q && out_ok) {
       // heap sort of the st.size entries -> ascending (distance, index);
       // the rest of the list is padding
+      const HeapStore<kC> heap = heap_of<kC>(sm);
       const int n = st.size;
       for (int end = n - 1; end > 0; --end) {
-        const uint64_t top = sm.heap[row];
-        const uint64_t last = sm.heap[end * stride + row];
-        sm.heap[end * stride + row] = top;
-        heap_sift_down(sm.heap, end, stride, row, 0, last, k, p.err);
+        const uint64_t top = heap.get(row);
+        const uint64_t last = heap.get(end * stride + row);
+        heap.set(end * stride + row, top);
+        heap_sift_down(heap, end, stride, row, 0, last, k, p.err);
       }
       const int s = u / p.query_tiles;
       float* od = p.part_d + (static_cast<size_t>(q) * p.splits + s) * k;
       uint32_t* oi = p.part_i + (static_cast<size_t>(q) * p.splits + s) * k;
       for (int r = 0; r < k; ++r) {
-        const uint64_t key = r < n ? sm.heap[r * stride + row] : empty_key<kMetric>();
+        const uint64_t key = r < n ? heap.get(r * stride + row) : empty_key<kMetric>();
         od[r] = key_dist<kMetric>(key);
-        oi[r] = static_cast<uint32_t>(key);
+        oi[r] = r < n && kC ? base + static_cast<uint32_t>(key) : static_cast<uint32_t>(key);
       }
     }
   }
 }
 
-template <int kMetric, bool kReg, bool kPair>
+template <int kMetric, bool kReg, bool kC, bool kPair>
 __global__ void __launch_bounds__(kScanThreads, 1)
     knn_scan_kernel(const __grid_constant__ CUtensorMap qmap,
                     const __grid_constant__ CUtensorMap xmap,
@@ -833,7 +879,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
   } else if (warp == 1) {
     if (lane == 0 && (!kPair || cluster_ctarank() == 0)) mma_issuer<kPair>(p, sm, tmem_base);
   } else {
-    epilogue<kMetric, kReg, kPair>(p, sm, tmem_base, warp, lane);
+    epilogue<kMetric, kReg, kC, kPair>(p, sm, tmem_base, warp, lane);
   }
 
   tc_fence_before();
@@ -929,7 +975,11 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
   if (n_rows <= 0 || dim <= 0 || n_queries <= 0 || k <= 0 || !out) return 1;
   if (k > kMaxK) return 6;
   if (num_sms <= 0) num_sms = 148;
-  const int64_t heap_per_query = (k + kRowBuf) * 8;  // heap + survivor buffer
+  (void)dim;
+  // shared memory per query row: its top-k (full 8-byte keys, or compact
+  // 6-byte entries for k > kRegK) and its survivor buffer
+  const int64_t heap_full = (k + kRowBuf) * 8;
+  const int64_t heap_compact = k * 6 + kRowBuf * 8;
   const int64_t budget = kSmemLimit - kSmemReserve;
   const int64_t row_tiles = (n_rows + kTileRows - 1) / kTileRows;
   *out = Plan{};
@@ -955,14 +1005,18 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
     }
     return best_s;
   };
+  // compact heaps need units of at most kCompactMaxRows rows
+  auto compact_fits = [&](int64_t n_gran, int64_t gran, int64_t splits) {
+    return k > kRegK && (n_gran + splits - 1) / splits * gran <= kCompactMaxRows;
+  };
   // More than one 128-query tile and heaps so large (k >= 62) that one CTA
   // would keep fewer than 3 pipeline stages: CTA pairs (M = 256 over two
   // SMs, each loading half of every dataset tile into stages of 32 KiB
   // instead of 48).  Measured on one B200: Q = 10,000, K = 100 over 1.25M
   // rows 32.2 -> 28.7 ms; with 4 stages already (K = 10) pairs were 6%
   // slower, so smaller k stays on single CTAs.
-  const int64_t pair_stages = (budget - kQueryRows * heap_per_query) / stage_bytes(1);
-  const int64_t single_stages = (budget - kQueryRows * heap_per_query) / kStageBytes;
+  const int64_t pair_stages = (budget - kQueryRows * heap_full) / stage_bytes(1);
+  const int64_t single_stages = (budget - kQueryRows * heap_full) / kStageBytes;
   if (n_queries > kQueryRows && single_stages < 3 && pair_stages >= 2 && num_sms >= 2) {
     const int64_t gran = 2 * kGranRows;
     const int64_t n_gran = (n_rows + gran - 1) / gran;
@@ -971,47 +1025,73 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
     const int64_t splits = pick_splits(query_tiles, n_gran, gran, pairs);
     const int64_t units = query_tiles * splits;
     if (units > INT32_MAX || n_gran * gran > INT32_MAX + int64_t(kTileRows)) return 6;
-    const int64_t stages = pair_stages > kMaxStages ? kMaxStages : pair_stages;
+    // compact heaps where they buy a stage (K = 100: 3 -> 4 stages)
+    const int64_t compact_stages = (budget - kQueryRows * heap_compact) / stage_bytes(1);
+    const bool compact = compact_stages > pair_stages && compact_fits(n_gran, gran, splits);
+    int64_t stages = compact ? compact_stages : pair_stages;
+    if (stages > kMaxStages) stages = kMaxStages;
     out->query_block = kQueryRows;
     out->query_tiles = query_tiles;
     out->splits = splits;
     out->units = units;
     out->grid = 2 * (units < pairs ? units : pairs);
     out->stages = stages;
-    out->smem_bytes = kSmemReserve + stages * stage_bytes(1) + kQueryRows * heap_per_query;
+    out->smem_bytes = kSmemReserve + stages * stage_bytes(1) +
+                      kQueryRows * (compact ? heap_compact : heap_full);
     out->partial_bytes = n_queries * splits * k * 8;
     out->pair = 1;
+    out->compact = compact ? 1 : 0;
     out->gran_rows = gran;
     out->unit_queries = 2 * kQueryRows;
-    (void)dim;
     return 0;
   }
-  int64_t qb_cap = (budget - 2 * kStageBytes) / heap_per_query;
-  qb_cap = (qb_cap / 32) * 32;
-  if (qb_cap > kQueryRows) qb_cap = kQueryRows;
-  if (qb_cap < 32) return 6;
-  int64_t qb = ((n_queries + 31) / 32) * 32;
-  if (qb > qb_cap) qb = qb_cap;
-  int64_t stages = (budget - qb * heap_per_query) / kStageBytes;
-  if (stages > kMaxStages) stages = kMaxStages;
-  if (stages < 2) return 6;
-  const int64_t query_tiles = (n_queries + qb - 1) / qb;
+  // Single CTAs: the query block (rows per unit) and the stage count follow
+  // from the per-query footprint; compact heaps are used where they give
+  // more stages (or a larger query block with as many) and every unit fits
+  // them.
+  struct Single {
+    int64_t qb, stages, query_tiles, splits;
+  };
+  auto single = [&](int64_t per_query, Single* o) {
+    int64_t qb_cap = (budget - 2 * kStageBytes) / per_query;
+    qb_cap = (qb_cap / 32) * 32;
+    if (qb_cap > kQueryRows) qb_cap = kQueryRows;
+    if (qb_cap < 32) return false;
+    int64_t qb = ((n_queries + 31) / 32) * 32;
+    if (qb > qb_cap) qb = qb_cap;
+    int64_t stages = (budget - qb * per_query) / kStageBytes;
+    if (stages > kMaxStages) stages = kMaxStages;
+    if (stages < 2) return false;
+    o->qb = qb;
+    o->stages = stages;
+    o->query_tiles = (n_queries + qb - 1) / qb;
+    o->splits = pick_splits(o->query_tiles, (n_rows + kGranRows - 1) / kGranRows, kGranRows,
+                            num_sms);
+    return true;
+  };
   const int64_t n_gran = (n_rows + kGranRows - 1) / kGranRows;
-  const int64_t splits = pick_splits(query_tiles, n_gran, kGranRows, num_sms);
-  const int64_t units = query_tiles * splits;
+  Single full{}, cmp{};
+  const bool full_ok = single(heap_full, &full);
+  const bool cmp_ok = k > kRegK && single(heap_compact, &cmp) &&
+                      compact_fits(n_gran, kGranRows, cmp.splits) &&
+                      (!full_ok || cmp.stages > full.stages ||
+                       (cmp.qb > full.qb && cmp.stages >= full.stages));
+  if (!full_ok && !cmp_ok) return 6;
+  const Single& c = cmp_ok ? cmp : full;
+  const int64_t units = c.query_tiles * c.splits;
   if (units > INT32_MAX || n_gran * kGranRows > INT32_MAX + int64_t(kTileRows)) return 6;
-  out->query_block = qb;
-  out->query_tiles = query_tiles;
-  out->splits = splits;
+  out->query_block = c.qb;
+  out->query_tiles = c.query_tiles;
+  out->splits = c.splits;
   out->units = units;
   out->grid = units < num_sms ? units : num_sms;
-  out->stages = stages;
-  out->smem_bytes = kSmemReserve + stages * kStageBytes + qb * heap_per_query;
-  out->partial_bytes = n_queries * splits * k * 8;
+  out->stages = c.stages;
+  out->smem_bytes = kSmemReserve + c.stages * kStageBytes + c.qb * (cmp_ok ? heap_compact : heap_full);
+  out->partial_bytes = n_queries * c.splits * k * 8;
   out->pair = 0;
+  out->compact = cmp_ok ? 1 : 0;
   out->gran_rows = kGranRows;
-  out->unit_queries = qb;
-  (void)dim;
+  out->unit_queries = c.qb;
   return 0;
 }
 
@@ -1026,13 +1106,14 @@ cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
   if (p.metric != KNN_METRIC_L2_EXPANDED && p.metric != KNN_METRIC_INNER_PRODUCT)
     return cudaErrorInvalidValue;
   const bool ip = p.metric == KNN_METRIC_INNER_PRODUCT;
-#define KNN_SCAN_FNS(M)                                                          \
-  reinterpret_cast<const void*>(knn_scan_kernel<M, false, false>),              \
-      reinterpret_cast<const void*>(knn_scan_kernel<M, true, false>),           \
-      reinterpret_cast<const void*>(knn_scan_kernel<M, false, true>),           \
-      reinterpret_cast<const void*>(knn_scan_kernel<M, true, true>)
-  static const void* const fns[8] = {KNN_SCAN_FNS(KNN_METRIC_L2_EXPANDED),
-                                     KNN_SCAN_FNS(KNN_METRIC_INNER_PRODUCT)};
+  // [metric][pair][top-k kind: full-key heap, registers, compact heap]
+#define KNN_SCAN_FNS(M, P)                                                       \
+  reinterpret_cast<const void*>(knn_scan_kernel<M, false, false, P>),           \
+      reinterpret_cast<const void*>(knn_scan_kernel<M, true, false, P>),        \
+      reinterpret_cast<const void*>(knn_scan_kernel<M, false, true, P>)
+  static const void* const fns[12] = {
+      KNN_SCAN_FNS(KNN_METRIC_L2_EXPANDED, false), KNN_SCAN_FNS(KNN_METRIC_L2_EXPANDED, true),
+      KNN_SCAN_FNS(KNN_METRIC_INNER_PRODUCT, false), KNN_SCAN_FNS(KNN_METRIC_INNER_PRODUCT, true)};
 #undef KNN_SCAN_FNS
   if (dev < 0 || dev >= 64 || !configured[dev]) {
     for (const void* fn : fns) {
@@ -1042,8 +1123,12 @@ cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
     }
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
+  // compact heaps: rebased row offsets fit 16 bits in every unit
+  const bool compact_ok =
+      p.k > kRegK && (p.n_gran + p.splits - 1) / p.splits * p.gran_rows <= kCompactMaxRows;
   if (p.n_gran != (p.n_rows + p.gran_rows - 1) / p.gran_rows || p.splits < 1 ||
       p.splits > p.n_gran || (p.pair != 0) != (plan.pair != 0) ||
+      (p.compact != 0) != (plan.compact != 0) || (p.compact && !compact_ok) ||
       (p.pair && (plan.grid % 2 != 0 || p.gran_rows != 2 * kGranRows ||
                   p.unit_queries != 2 * kQueryRows || p.query_block != kQueryRows)))
     return cudaErrorInvalidValue;
@@ -1063,7 +1148,7 @@ cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
   cfg.numAttrs = p.pair ? 2 : 1;
   // small k: the register top-k (the pilot pass only runs for k > kRegK)
   const bool reg = p.k <= kRegK && !p.pilot;
-  const void* fn = fns[(ip ? 4 : 0) + (p.pair ? 2 : 0) + (reg ? 1 : 0)];
+  const void* fn = fns[(ip ? 6 : 0) + (p.pair ? 3 : 0) + (reg ? 1 : (p.compact ? 2 : 0))];
   void* args[] = {const_cast<CUtensorMap*>(&qmap), const_cast<CUtensorMap*>(&xmap),
                   const_cast<CUtensorMap*>(&xmap_tail), const_cast<ScanParams*>(&p)};
   return cudaLaunchKernelExC(&cfg, fn, args);

@@ -48,7 +48,8 @@ MAX_K = 256
 class KnnPlan(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int64) for n in (
         "query_block", "query_tiles", "row_tiles", "splits", "units", "grid",
-        "stages", "smem_bytes", "partial_bytes", "pair", "unit_queries")]
+        "stages", "smem_bytes", "partial_bytes", "pair", "unit_queries",
+        "compact_heap")]
 
 
 _lib = None

@@ -90,6 +90,7 @@ typedef struct knn_plan {
   int64_t partial_bytes; /* scratch for per-unit top-k lists */
   int64_t pair;          /* 1: pairs of CTAs share each dataset tile (cta_group::2) */
   int64_t unit_queries;  /* queries per work unit (query_block, or 256 with pairs) */
+  int64_t compact_heap;  /* 1: k > 16 top-k heaps of 6-byte entries (units of <= 65535 rows) */
 } knn_plan;
 
 /* Human-readable text for the calling thread's last failure. */

@@ -40,6 +40,7 @@ def main():
         (4097, 128, 130, 32, 0), (20011, 100, 37, 100, 0), (3000, 200, 300, 10, 0),
         (600, 96, 5, 256, 0), (9000, 64, 64, 10, 1), (777, 130, 9, 50, 1),
         (20011, 72, 257, 64, 0), (3001, 200, 600, 100, 1),  # CTA pairs
+        (1000, 128, 100, 64, 0), (700, 64, 300, 100, 0),  # compact heaps
     ]
     for n, dim, nq, k, metric in cases:
         base = rng.standard_normal((n, dim), dtype=np.float32)

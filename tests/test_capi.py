@@ -68,6 +68,23 @@ def test_planner_fits_shared_memory(engine, nq, k):
     assert p["units"] == p["query_tiles"] * p["splits"]
     assert 1 <= p["splits"] <= p["row_tiles"]
     assert p["grid"] == min(p["units"], 148)
+    if p["compact_heap"]:
+        gran = 64 if p["pair"] else 32
+        n_gran = -(-1_000_000 // gran)
+        assert k > 16 and -(-n_gran // p["splits"]) * gran <= 65535
+
+
+def test_planner_compact_heaps(engine):
+    # compact 6-byte heap entries where they buy a pipeline stage and every
+    # unit spans at most 65,535 rows; full keys otherwise
+    c4 = engine.plan_search(1_250_000, 1024, 10_000, 100)
+    assert c4["pair"] == 1 and c4["compact_heap"] == 1 and c4["stages"] == 4
+    big = engine.plan_search(10_000_000, 1024, 10_000, 100)
+    assert big["pair"] == 1 and big["compact_heap"] == 0 and big["stages"] == 3
+    single = engine.plan_search(1_000_000, 1024, 100, 64)
+    assert single["pair"] == 0 and single["compact_heap"] == 1 and single["stages"] == 3
+    assert engine.plan_search(1_000_000, 1024, 100, 10)["compact_heap"] == 0
+    assert engine.plan_search(1_000_000, 1024, 16, 256)["compact_heap"] == 0
 
 
 def test_planner_limits(engine):

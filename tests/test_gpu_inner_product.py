@@ -89,6 +89,7 @@ SHAPES = [
     (4099, 256, 16, 256),
     (700, 64, 300, 100),
     (20011, 72, 257, 64),
+    (1000, 128, 100, 64),
 ]
 
 

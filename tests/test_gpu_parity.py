@@ -131,6 +131,12 @@ SHAPES = [
     (20011, 72, 257, 64),
     (130, 33, 129, 62),
     (3001, 200, 600, 128),
+    # compact 6-byte heap entries (k > 16 where they buy a stage): single
+    # CTAs at k = 64, and CTA pairs whose units span 62,163 rows (row
+    # offsets near the 16-bit limit)
+    (1000, 128, 100, 64),
+    (50000, 64, 100, 64),
+    (2300000, 16, 260, 100),
 ]
 
 
