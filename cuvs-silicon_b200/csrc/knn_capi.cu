@@ -228,6 +228,7 @@ struct knn_index {
   float* norms = nullptr;
   CUtensorMap xmap;       // 256-row boxes (full tiles)
   CUtensorMap xmap_tail;  // 32-row boxes (a work unit's narrower last tile)
+  CUtensorMap xmap_half;  // 128-row boxes (a CTA's half of a full tile with CTA pairs)
 
   // exact fp32 re-ranking (knn_index_set_rerank): the fp32 rows are kept
   // by a build made while re-ranking is enabled
@@ -598,7 +599,7 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
     // distance, and the main pass filters with that bound from its first tile
     p.pilot = 1;
     p.pilot_out = h->pilot.as<float>();
-    KNN_CUDA(knn::launch_scan(qmap, h->xmap, h->xmap_tail, p, plan, h->stream, overlap));
+    KNN_CUDA(knn::launch_scan(qmap, h->xmap, h->xmap_tail, h->xmap_half, p, plan, h->stream, overlap));
     KNN_CUDA(knn::launch_pilot_threshold(p.pilot_out, static_cast<int>(plan.splits),
                                          static_cast<int>(ks), nq, h->thr.as<float>(),
                                          h->stream));
@@ -608,7 +609,7 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
     launches += 2;
   }
   p.bound = h->bound.as<uint32_t>();
-  KNN_CUDA(knn::launch_scan(qmap, h->xmap, h->xmap_tail, p, plan, h->stream, overlap));
+  KNN_CUDA(knn::launch_scan(qmap, h->xmap, h->xmap_tail, h->xmap_half, p, plan, h->stream, overlap));
   if (prof) KNN_CUDA(cudaEventRecord((*prof)[1], h->stream));
 
   // the lists the final stage merges: the scan's per-unit lists, or one
@@ -998,6 +999,7 @@ int build_impl(knn_index* h, const void* rows, int dtype, int64_t n, int64_t dim
   KNN_CUDA(cudaStreamSynchronize(h->stream));
   int st = encode_rows(&h->xmap, h->data, n, ld, knn::kTileRows);
   if (st == KNN_OK) st = encode_rows(&h->xmap_tail, h->data, n, ld, knn::kTailBox);
+  if (st == KNN_OK) st = encode_rows(&h->xmap_half, h->data, n, ld, knn::kTileRows / 2);
   if (st != KNN_OK) return st;
   ++h->generation;
   drop_graphs(h);
@@ -1053,6 +1055,7 @@ int build_prepared_impl(knn_index* h, const void* rows16, const float* norms, in
   KNN_CUDA(cudaStreamSynchronize(h->stream));
   int st = encode_rows(&h->xmap, h->data, n, ld, knn::kTileRows);
   if (st == KNN_OK) st = encode_rows(&h->xmap_tail, h->data, n, ld, knn::kTailBox);
+  if (st == KNN_OK) st = encode_rows(&h->xmap_half, h->data, n, ld, knn::kTileRows / 2);
   if (st != KNN_OK) return st;
   ++h->generation;
   drop_graphs(h);
@@ -1223,6 +1226,7 @@ int build_file_impl(knn_index* h, const char* path, int format, int metric, int 
   cleanup();
   if (st == KNN_OK) st = encode_rows(&h->xmap, h->data, n, ld, knn::kTileRows);
   if (st == KNN_OK) st = encode_rows(&h->xmap_tail, h->data, n, ld, knn::kTailBox);
+  if (st == KNN_OK) st = encode_rows(&h->xmap_half, h->data, n, ld, knn::kTileRows / 2);
   if (st != KNN_OK) {
     cudaFree(h->data);
     cudaFree(h->norms);
@@ -1806,7 +1810,7 @@ int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
   p.pilot_out = nullptr;
   p.thr_init = nullptr;
   p.bound = nullptr;
-  KNN_CUDA(knn::launch_scan(qmap, h->xmap, h->xmap_tail, p, plan, h->stream));
+  KNN_CUDA(knn::launch_scan(qmap, h->xmap, h->xmap_tail, h->xmap_half, p, plan, h->stream));
   KNN_CUDA(knn::launch_merge(part_d, part_i, k, plan.splits * k, static_cast<int>(plan.splits),
                              static_cast<int>(k), nq, h->row_offset, out_d, out_i, false,
                              h->stream, true, nullptr,

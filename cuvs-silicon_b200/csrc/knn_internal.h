@@ -106,10 +106,13 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
 // before it (its set-up overlaps that kernel's tail); off when the caller
 // brackets kernels with timing events.  xmap: the dataset rows with
 // kTileRows-row boxes; xmap_tail: the same rows with kTailBox-row boxes (a
-// unit's last tile is loaded as several of these).
+// unit's last tile is loaded as several of these); xmap_half: the same rows
+// with kTileRows / 2-row boxes (each CTA's half of a full tile with CTA
+// pairs).
 cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
-                        const CUtensorMap& xmap_tail, const ScanParams& p, const Plan& plan,
-                        cudaStream_t stream, bool overlap = true);
+                        const CUtensorMap& xmap_tail, const CUtensorMap& xmap_half,
+                        const ScanParams& p, const Plan& plan, cudaStream_t stream,
+                        bool overlap = true);
 
 // fp32/fp16 rows -> fp16 rows with leading dimension ld (zero padded) plus
 // fp32 norms of the rounded rows.  in_is_half selects the input type.

@@ -234,7 +234,8 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
 // swizzle atom).
 template <bool kPair>
 __device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap,
-                         const CUtensorMap* xmap_tail, const ScanParams& p, const Smem& sm) {
+                         const CUtensorMap* xmap_tail, const CUtensorMap* xmap_half,
+                         const ScanParams& p, const Smem& sm) {
   const uint64_t pol_q = policy_evict_last();
   const uint64_t pol_x = p.dataset_evict_first ? policy_evict_first() : policy_evict_normal();
   const uint32_t crank = kPair ? cluster_ctarank() : 0u;
@@ -267,6 +268,8 @@ __device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap,
       return;
     if (!kPair && w == kTileRows) {
       load(dst, xmap, slot, kc * kKChunk, static_cast<int32_t>(r0), pol_x);
+    } else if (kPair && w == kTileRows) {
+      load(dst, xmap_half, slot, kc * kKChunk, static_cast<int32_t>(r0), pol_x);
     } else {
       for (int j = 0; j < h; j += kTailBox)
         load(dst + j * (kKChunk * 2), xmap_tail, slot, kc * kKChunk,
@@ -825,7 +828,8 @@ template <int kMetric, bool kReg, bool kC, bool kPair>
 __global__ void __launch_bounds__(kScanThreads, 1)
     knn_scan_kernel(const __grid_constant__ CUtensorMap qmap,
                     const __grid_constant__ CUtensorMap xmap,
-                    const __grid_constant__ CUtensorMap xmap_tail, const ScanParams p) {
+                    const __grid_constant__ CUtensorMap xmap_tail,
+                    const __grid_constant__ CUtensorMap xmap_half, const ScanParams p) {
   extern __shared__ uint8_t smem_raw[];
   const Smem sm = carve(smem_raw, p);
   const int warp = threadIdx.x >> 5;
@@ -850,6 +854,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     tma_prefetch_map(&qmap);
     tma_prefetch_map(&xmap);
     tma_prefetch_map(&xmap_tail);
+    if constexpr (kPair) tma_prefetch_map(&xmap_half);
   }
   if (warp == 1) {
     if constexpr (kPair) {
@@ -875,7 +880,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
-    if (lane == 0) producer<kPair>(&qmap, &xmap, &xmap_tail, p, sm);
+    if (lane == 0) producer<kPair>(&qmap, &xmap, &xmap_tail, &xmap_half, p, sm);
   } else if (warp == 1) {
     if (lane == 0 && (!kPair || cluster_ctarank() == 0)) mma_issuer<kPair>(p, sm, tmem_base);
   } else {
@@ -1096,8 +1101,9 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
 }
 
 cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
-                        const CUtensorMap& xmap_tail, const ScanParams& p, const Plan& plan,
-                        cudaStream_t stream, bool overlap) {
+                        const CUtensorMap& xmap_tail, const CUtensorMap& xmap_half,
+                        const ScanParams& p, const Plan& plan, cudaStream_t stream,
+                        bool overlap) {
   // the opt-in shared-memory limit is a per-device function attribute
   static std::atomic<bool> configured[64] = {};  // set once; idempotent
   int dev = 0;
@@ -1150,7 +1156,8 @@ cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
   const bool reg = p.k <= kRegK && !p.pilot;
   const void* fn = fns[(ip ? 6 : 0) + (p.pair ? 3 : 0) + (reg ? 1 : (p.compact ? 2 : 0))];
   void* args[] = {const_cast<CUtensorMap*>(&qmap), const_cast<CUtensorMap*>(&xmap),
-                  const_cast<CUtensorMap*>(&xmap_tail), const_cast<ScanParams*>(&p)};
+                  const_cast<CUtensorMap*>(&xmap_tail), const_cast<CUtensorMap*>(&xmap_half),
+                  const_cast<ScanParams*>(&p)};
   return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
