@@ -1014,15 +1014,24 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
   auto compact_fits = [&](int64_t n_gran, int64_t gran, int64_t splits) {
     return k > kRegK && (n_gran + splits - 1) / splits * gran <= kCompactMaxRows;
   };
-  // More than one 128-query tile and heaps so large (k >= 62) that one CTA
-  // would keep fewer than 3 pipeline stages: CTA pairs (M = 256 over two
-  // SMs, each loading half of every dataset tile into stages of 32 KiB
-  // instead of 48).  Measured on one B200: Q = 10,000, K = 100 over 1.25M
-  // rows 32.2 -> 28.7 ms; with 4 stages already (K = 10) pairs were 6%
-  // slower, so smaller k stays on single CTAs.
+  // CTA pairs (M = 256 over two SMs, each loading half of every dataset
+  // tile into stages of 32 KiB instead of 48) for more than one 128-query
+  // tile when either
+  //   * the heaps are so large (k >= 62) that one CTA would keep fewer than
+  //     3 pipeline stages, or
+  //   * pairs pad the queries by at most 5% more rows than single CTAs do
+  //     (256-query units against 128).
+  // Same-box A/B on one B200, byte-identical results: Q = 10,000, K = 100
+  // over 1.25M rows 32.2 -> 28.7 ms; K = 10: Q = 2000 over 200k rows 763 ->
+  // 724 us, Q = 10,000 over 1.25M rows 25.7 -> 24.7 ms, Q = 129 over 1M rows
+  // 565 -> 481 us; but Q = 300 (512 padded rows against 384) 768 -> 922 us.
+  const int64_t single_rows = (n_queries + kQueryRows - 1) / kQueryRows * kQueryRows;
+  const int64_t pair_rows = (n_queries + 2 * kQueryRows - 1) / (2 * kQueryRows) * 2 * kQueryRows;
+  const bool pair_pays = 20 * pair_rows <= 21 * single_rows;
   const int64_t pair_stages = (budget - kQueryRows * heap_full) / stage_bytes(1);
   const int64_t single_stages = (budget - kQueryRows * heap_full) / kStageBytes;
-  if (n_queries > kQueryRows && single_stages < 3 && pair_stages >= 2 && num_sms >= 2) {
+  if (n_queries > kQueryRows && (single_stages < 3 || pair_pays) && pair_stages >= 2 &&
+      num_sms >= 2) {
     const int64_t gran = 2 * kGranRows;
     const int64_t n_gran = (n_rows + gran - 1) / gran;
     const int64_t query_tiles = (n_queries + 2 * kQueryRows - 1) / (2 * kQueryRows);

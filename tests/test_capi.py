@@ -54,20 +54,24 @@ def test_planner_headline(engine):
 
 
 @pytest.mark.parametrize("nq,k", [(1, 10), (16, 256), (100, 256), (10000, 100),
-                                  (1, 256), (33, 1), (100, 100)])
+                                  (1, 256), (33, 1), (100, 100), (129, 10), (300, 10),
+                                  (1000, 10), (10000, 10), (600, 32), (200, 32)])
 def test_planner_fits_shared_memory(engine, nq, k):
     p = engine.plan_search(1_000_000, 1024, nq, k)
     assert p["smem_bytes"] <= 232448
     assert p["stages"] >= 2
     assert p["query_block"] % 32 == 0 and 32 <= p["query_block"] <= 128
     assert p["query_tiles"] * p["unit_queries"] >= nq
-    # CTA pairs only where one CTA would keep fewer than 3 stages (k >= 62)
-    assert p["pair"] == (1 if nq > 128 and k >= 62 else 0), p
+    # CTA pairs for more than 128 queries where one CTA would keep fewer
+    # than 3 stages (k >= 62) or pairs pad the queries by at most 5% more
+    single_rows, pair_rows = -(-nq // 128) * 128, -(-nq // 256) * 256
+    want = nq > 128 and (k >= 62 or 20 * pair_rows <= 21 * single_rows)
+    assert p["pair"] == (1 if want else 0), p
     if p["pair"]:
         assert p["grid"] % 2 == 0 and p["unit_queries"] == 256 and p["query_block"] == 128
     assert p["units"] == p["query_tiles"] * p["splits"]
     assert 1 <= p["splits"] <= p["row_tiles"]
-    assert p["grid"] == min(p["units"], 148)
+    assert p["grid"] == (2 * min(p["units"], 74) if p["pair"] else min(p["units"], 148))
     if p["compact_heap"]:
         gran = 64 if p["pair"] else 32
         n_gran = -(-1_000_000 // gran)

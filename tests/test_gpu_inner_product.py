@@ -90,6 +90,7 @@ SHAPES = [
     (700, 64, 300, 100),
     (20011, 72, 257, 64),
     (1000, 128, 100, 64),
+    (20011, 64, 1000, 16),
 ]
 
 

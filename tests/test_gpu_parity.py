@@ -137,6 +137,10 @@ SHAPES = [
     (1000, 128, 100, 64),
     (50000, 64, 100, 64),
     (2300000, 16, 260, 100),
+    # CTA pairs at small k (query padding no worse than single CTAs'):
+    # register top-k, several pair tiles, and the pilot pass at k = 32
+    (20011, 64, 1000, 16),
+    (1000, 128, 200, 32),
 ]
 
 
