@@ -183,6 +183,54 @@ __device__ __forceinline__ void block_sort(float* d, uint32_t* i, int p2) {
   }
 }
 
+// Order-preserving 32-bit image of a distance (-0 counted as +0, which the
+// (distance, index) order treats as equal).
+__device__ __forceinline__ uint32_t order_key(float d) {
+  const uint32_t u = __float_as_uint(d == 0.0f ? 0.0f : d);
+  return u ^ ((u >> 31) ? 0xFFFFFFFFu : 0x80000000u);
+}
+
+// The image (order_key) of the k-th smallest of d[0..n), 1 <= k <= n, by a
+// radix select: four passes over the 8-bit digits from the top, each a
+// shared-memory histogram of the entries that match the digits chosen so far
+// and a block scan that finds the digit holding the k-th.  blockDim.x ==
+// 256 (one histogram bin per thread); hist: 256 ints, misc: 10 ints.
+// Called by every thread; ends with a block barrier.
+__device__ uint32_t block_select_kth(const float* d, int n, int k, int* hist, int* misc) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t prefix = 0, mask = 0;
+  int want = k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    hist[tid] = 0;
+    __syncthreads();
+    for (int e = tid; e < n; e += blockDim.x) {
+      const uint32_t key = order_key(d[e]);
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
+    }
+    __syncthreads();
+    const int h = hist[tid];
+    int incl = h;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) misc[warp] = incl;
+    __syncthreads();
+    for (int w = 0; w < warp; ++w) incl += misc[w];
+    if (incl - h < want && want <= incl) {  // exactly one bin
+      misc[8] = tid;
+      misc[9] = incl - h;
+    }
+    __syncthreads();
+    want -= misc[9];
+    prefix |= static_cast<uint32_t>(misc[8]) << shift;
+    mask |= 255u << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
 // Sorts n <= blockDim.x entries by rank counting: thread t takes entry t,
 // counts the entries ordered before it (one broadcast shared-memory read per
 // entry, no barrier in between) and stores it at that rank in out_d/out_i,
@@ -443,26 +491,52 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
   const int total = n_lists * k;
   constexpr int kPer = 8;  // entries per thread per round, loaded before use
   if (n_lists <= static_cast<int>(blockDim.x) && k > kLongList) {
-    // Long lists: thread l finds the length of list l's prefix <= tau by
-    // binary search (about log2 k dependent loads instead of a walk of up to
-    // k), a block scan turns the lengths into offsets, and all threads copy
-    // the candidates together.  The offsets reuse the selection array
-    // (tau is already in registers).
+    // Long lists: the length of each list's prefix <= tau, found by the
+    // warps: warp w takes lists w, w + 8, ... in batches of kPrefixBatch,
+    // lane e reading entry e of every list of the batch (independent loads,
+    // one memory round per batch); a list's prefix length is the popcount
+    // of the ballot of its entries <= tau, extended 32 entries at a time in
+    // the rare case that all 32 pass.  A block scan then turns the lengths
+    // into offsets and all threads copy the candidates together.  The
+    // offsets reuse the selection array (tau is already in registers).
     int* off = reinterpret_cast<int*>(seli);  // [n_lists + 1]
-    int len = 0;
-    if (tid < n_lists) {
-      const float* lsd = qd + static_cast<int64_t>(tid) * stride_list;
-      const uint32_t* lsi = qi + static_cast<int64_t>(tid) * stride_list;
-      int lo = 0, hi = k;  // entries [0, lo) are <= tau, [hi, k) are not
-      while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        const float dm = lsd[mid];
-        const uint32_t im = lsi[mid];
-        if (im != kNoIndex && (dm < td || (dm == td && im <= ti))) lo = mid + 1;
-        else hi = mid;
+    constexpr int kPrefixBatch = 8;
+    const int warp = tid >> 5;
+    auto passes = [&](float dm, uint32_t im) {
+      return im != kNoIndex && (dm < td || (dm == td && im <= ti));
+    };
+    for (int l0 = warp; l0 < n_lists; l0 += kMergeWarps * kPrefixBatch) {
+      float dv[kPrefixBatch];
+      uint32_t iv[kPrefixBatch];
+#pragma unroll
+      for (int b = 0; b < kPrefixBatch; ++b) {
+        const int l = l0 + b * kMergeWarps;
+        dv[b] = 0.0f;
+        iv[b] = kNoIndex;
+        if (l < n_lists && lane < k) {
+          const int64_t at = static_cast<int64_t>(l) * stride_list + lane;
+          iv[b] = qi[at];
+          dv[b] = qd[at];
+        }
       }
-      len = lo;
+#pragma unroll
+      for (int b = 0; b < kPrefixBatch; ++b) {
+        const int l = l0 + b * kMergeWarps;  // warp-uniform
+        if (l >= n_lists) continue;
+        unsigned m = __ballot_sync(0xffffffffu, passes(dv[b], iv[b]));
+        int len = __popc(m);
+        for (int e0 = 32; m == 0xffffffffu && e0 < k; e0 += 32) {
+          const int e = e0 + lane;
+          const int64_t at = static_cast<int64_t>(l) * stride_list + e;
+          const bool p = e < k && passes(qd[at], qi[at]);
+          m = __ballot_sync(0xffffffffu, p);
+          len += __popc(m);
+        }
+        if (lane == 0) off[l] = len;
+      }
     }
+    __syncthreads();
+    const int len = tid < n_lists ? off[tid] : 0;
     // exclusive scan of the lengths: warp scans, then the warp totals
     __shared__ int s_warp[kMergeWarps];
     int incl = len;
@@ -574,6 +648,40 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
     emit_result(ex, push, epoch, q, k, seld, seli, count, index_offset, out_d, out_i, sign);
     return;
   }
+  if (count > 2 * kRankPlaceLong) {
+    // Many candidates (a loose tau, or none when fewer than r lists hold j
+    // entries): the k-th smallest distance D by a radix select, then only
+    // the entries at or below D (k of them, more only with ties at D) are
+    // ordered, by rank counting.  Up to 512 candidates the block-wide sort
+    // is as fast (same-box A/B: K = 200, ~340 candidates, 20.5 us sorted
+    // against 22.5 us selected; K = 256, ~570 candidates, 26.6 -> 24.4 us).
+    // With ~3,800 candidates (tau the padding) a traced search spent 88 to
+    // 160 us per query block in the 4096-entry sort; with the select the
+    // whole search (125k rows, Q = 16, K = 256) went 130.7 -> 116.1 us.
+    __shared__ int s_hist[kMergeWarps * 32];
+    __shared__ int s_misc[10];
+    const uint32_t kth = block_select_kth(cd, count, k, s_hist, s_misc);
+    if (tid == 0) s_count = 0;
+    __syncthreads();
+    for (int e = tid; e < count; e += blockDim.x) {
+      if (order_key(cd[e]) <= kth) {
+        const int pos = atomicAdd(&s_count, 1);
+        if (pos < kSelCap) {
+          seld[pos] = cd[e];
+          seli[pos] = ci[e];
+        }
+      }
+    }
+    __syncthreads();
+    const int m = s_count;  // >= k
+    if (m <= kSelCap && m <= kRankPlaceLong) {
+      rank_place(seld, seli, m, cd, ci, k);
+      emit_result(ex, push, epoch, q, k, cd, ci, k, index_offset, out_d, out_i, sign);
+      return;
+    }
+  }
+  // at most 512 candidates, or more than 256 ties at the k-th distance:
+  // sort every candidate
   int c2 = 1;
   while (c2 < count) c2 <<= 1;
   for (int e = count + tid; e < c2; e += blockDim.x) {
@@ -586,7 +694,7 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
 }
 
 template <int E, typename OutIdx>
-__global__ void __launch_bounds__(kMergeWarps * 32)
+__global__ void __launch_bounds__(kMergeWarps * 32, 4)
     merge_kernel(const float* __restrict__ in_d, const uint32_t* __restrict__ in_i,
                  int64_t stride_list, int64_t stride_query, int n_lists, int k,
                  int64_t index_offset, float* __restrict__ out_d, OutIdx* __restrict__ out_i,
