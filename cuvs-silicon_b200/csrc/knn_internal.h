@@ -37,6 +37,7 @@ constexpr int kErrTimeoutAccFull = 3;   // epilogue waiting for an accumulator
 constexpr int kErrTimeoutAccEmpty = 4;  // MMA waiting for the epilogue
 constexpr int kErrTimeoutDrain = 5;     // unwinding waits
 constexpr int kErrBounds = 6;           // debug build: a bounds check tripped
+constexpr int kErrTimeoutEpilogue = 8;  // an epilogue warp waiting for the others
 
 struct ScanParams {
   const float* row_norms;    // [n_rows]

@@ -156,6 +156,7 @@ struct Smem {
   uint64_t* acc_full;
   uint64_t* acc_empty;
   uint64_t* drain;
+  uint64_t* epi_bar;  // the 4 epilogue warps meet here around a unit's list sort
   uint32_t* tmem_slot;
 };
 
@@ -186,7 +187,8 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, const ScanParams& p) {
   s.acc_full = bars + 2 * p.stages;
   s.acc_empty = s.acc_full + 2;
   s.drain = s.acc_empty + 2;
-  s.tmem_slot = reinterpret_cast<uint32_t*>(s.drain + 1);
+  s.epi_bar = s.drain + 1;
+  s.tmem_slot = reinterpret_cast<uint32_t*>(s.epi_bar + 1);
   return s;
 }
 
@@ -462,6 +464,10 @@ __device__ __forceinline__ void sort32(float (&g)[32]) { bitonic_sort<2>(g); }
 // sorted array of kRegK keys) instead of a shared-memory heap.
 constexpr int kRegK = 16;
 
+// Heap size from which a query block of 32 rows sorts its unit lists with
+// all 4 epilogue warps (warp-wide bitonic sorts) instead of lane by lane.
+constexpr int kCoopMinHeap = 64;
+
 // Per query row (one epilogue lane): the filter threshold, the worst kept
 // key (root), the number of buffered survivors and the top-k itself.
 // kReg: top[] holds kRegK keys in ascending order, the first kRegK - k of
@@ -538,6 +544,103 @@ __device__ __forceinline__ void flush_buffer(RowState<kReg>& st, const Smem& sm,
   st.thr = fminf(st.thr, key_dist<kMetric>(st.root));
 }
 
+// The 4 epilogue warps meet at sm.epi_bar (lane 0 of each arrives; every
+// lane waits, bounded).  `use` counts this warp's meetings (the barrier's
+// phase).  Returns false when the wait gave up (a warp that failed earlier
+// never arrives; its error word ends the wait).
+__device__ __forceinline__ bool epilogue_meet(const Smem& sm, uint32_t& use, int lane, int* err) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(sm.epi_bar);
+  const bool ok = mbar_wait(sm.epi_bar, use & 1u, err, kErrTimeoutEpilogue);
+  ++use;
+  return !__any_sync(0xffffffffu, !ok);
+}
+
+// Ascending bitonic sort of 32 * E keys held by one warp: element e lives in
+// register e / 32 of lane e % 32.  Strides of 32 and more compare registers
+// of the same lane, smaller ones exchange with lane ^ stride.
+template <int E>
+__device__ __forceinline__ void warp_sort_keys(uint64_t (&v)[E], int lane) {
+  constexpr int N = 32 * E;
+#pragma unroll
+  for (int size = 2; size <= N; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (stride >= 32) {
+        const int rs = stride / 32;
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+          if ((j & rs) == 0) {
+            const bool up = ((j * 32 + lane) & size) == 0;
+            const uint64_t a = v[j], b = v[j | rs];
+            const bool swap = up ? (b < a) : (a < b);
+            v[j] = swap ? b : a;
+            v[j | rs] = swap ? a : b;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+          const uint64_t o = __shfl_xor_sync(0xffffffffu, v[j], stride);
+          const bool up = ((j * 32 + lane) & size) == 0;
+          const bool lower = (lane & stride) == 0;
+          // the lower element of an ascending pair keeps the minimum
+          v[j] = (lower == up) ? (o < v[j] ? o : v[j]) : (o > v[j] ? o : v[j]);
+        }
+      }
+    }
+  }
+}
+
+// One query row's unit list from its heap: the warp loads the n heap
+// entries (padding: the empty key, above every real key), sorts them and
+// writes the first k as (distance, index), the index rebased for compact
+// heaps.
+template <int kMetric, bool kC, int E>
+__device__ __forceinline__ void write_sorted_row(const HeapStore<kC>& heap, int stride, int row,
+                                                 int n, int k, uint32_t base, float* od,
+                                                 uint32_t* oi, int lane) {
+  uint64_t v[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    const int e = j * 32 + lane;
+    v[j] = e < n ? heap.get(e * stride + row) : empty_key<kMetric>();
+  }
+  warp_sort_keys<E>(v, lane);
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    const int e = j * 32 + lane;
+    if (e < k) {
+      od[e] = key_dist<kMetric>(v[j]);
+      oi[e] = e < n ? (kC ? base + static_cast<uint32_t>(v[j]) : static_cast<uint32_t>(v[j]))
+                    : kNoIndex;
+    }
+  }
+}
+
+// The unit lists of a 32-row query block, row r sorted and written by
+// epilogue warp r % 4 (write_sorted_row).  Kept out of line so that its
+// registers do not weigh on the epilogue's tile loop.
+template <int kMetric, bool kC>
+__device__ __noinline__ void sort_rows_cooperative(const ScanParams& p, const HeapStore<kC> heap,
+                                                   const int* sizes, int m, int s, uint32_t base,
+                                                   int warp, int lane) {
+  const int k = p.k;
+  const int stride = p.query_block;
+  for (int r = warp - 2; r < p.query_block; r += 4) {  // warp-uniform
+    const int64_t qr = static_cast<int64_t>(m) * p.unit_queries + r;
+    if (qr >= p.n_queries || !in_bounds(s < p.splits, p.err)) continue;
+    const int n = sizes[r];
+    if (!in_bounds(n >= 0 && n <= k && r < stride, p.err)) continue;
+    float* od = p.part_d + (static_cast<size_t>(qr) * p.splits + s) * k;
+    uint32_t* oi = p.part_i + (static_cast<size_t>(qr) * p.splits + s) * k;
+    if (k <= 32) write_sorted_row<kMetric, kC, 1>(heap, stride, r, n, k, base, od, oi, lane);
+    else if (k <= 64) write_sorted_row<kMetric, kC, 2>(heap, stride, r, n, k, base, od, oi, lane);
+    else if (k <= 128) write_sorted_row<kMetric, kC, 4>(heap, stride, r, n, k, base, od, oi, lane);
+    else write_sorted_row<kMetric, kC, 8>(heap, stride, r, n, k, base, od, oi, lane);
+  }
+}
+
 // Epilogue warp.  Lane `row` owns query row `row` of the unit's query block.
 //
 // Candidate handling per 32-column chunk of an accumulator tile:
@@ -580,6 +683,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
   const int k = p.k;
   const float kInf = __int_as_float(0x7f800000);
   uint32_t tc = 0;
+  uint32_t meets = 0;  // epilogue_meet calls so far (the barrier's phase)
   bool failed = false;
   for (int u = first; u < p.units && !failed; u += step) {
     const Unit un = unit_of(p, u);
@@ -787,6 +891,34 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
     if (failed) break;
     if (p.pilot) continue;
     if (warp_active) flush_buffer<kMetric, kReg, kC>(st, sm, k, stride, row, base, p.err);
+    if (!kReg && p.query_block == kGranRows) {  // grid-uniform
+      // Query blocks of 32 rows: one warp owns every row and would sort
+      // each row's heap alone, lane by lane (a 256-entry heap sort costs
+      // tens of microseconds at the end of the unit).  Each owner leaves
+      // its row's heap size in its own norm-staging slice (free until its
+      // next tile); once the warps have met, all of them read the sizes,
+      // and if some heap holds kCoopMinHeap entries or more, row r is
+      // sorted by warp r % 4 with a warp-wide bitonic sort (a heap is in
+      // shared memory, so any warp can read it).  The warps meet again
+      // afterwards, so no owner refills a heap that another warp still
+      // reads.  Smaller heaps keep the per-lane sort below.
+      if (warp_active) reinterpret_cast<int*>(ns)[lane] = valid_q ? st.size : 0;
+      if (!epilogue_meet(sm, meets, lane, p.err)) {
+        failed = true;
+        break;
+      }
+      // rows 0-31 belong to TMEM lane quadrant 0, the warp of slice 2
+      const int* sizes = reinterpret_cast<const int*>(sm.norm_stage + 2 * kAccCols);
+      const bool coop = __reduce_max_sync(0xffffffffu, sizes[lane]) >= kCoopMinHeap;
+      if (coop)
+        sort_rows_cooperative<kMetric, kC>(p, heap_of<kC>(sm), sizes, un.m, u / p.query_tiles,
+                                           base, warp, lane);
+      if (!epilogue_meet(sm, meets, lane, p.err)) {
+        failed = true;
+        break;
+      }
+      if (coop) continue;
+    }
     const bool out_ok = !valid_q || in_bounds(q < p.n_queries && u / p.query_tiles < p.splits,
                                               p.err);
     if (kReg && valid_q && out_ok) {
@@ -848,6 +980,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
       mbar_init(&sm.acc_empty[b], kPair ? 8 : 4);
     }
     mbar_init(sm.drain, 1);
+    mbar_init(sm.epi_bar, 4);
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
