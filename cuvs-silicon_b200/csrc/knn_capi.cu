@@ -572,6 +572,7 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
   p.q_rows = nq_pad;
   p.pair = static_cast<int32_t>(plan.pair);
   p.compact = static_cast<int32_t>(plan.compact);
+  p.heap_rows = static_cast<int32_t>(plan.heap_rows);
   p.gran_rows = static_cast<int32_t>(plan.gran_rows);
   p.unit_queries = static_cast<int32_t>(plan.unit_queries);
   p.ld = h->ld;
@@ -1794,6 +1795,7 @@ int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
   p.q_rows = nq_pad;
   p.pair = static_cast<int32_t>(plan.pair);
   p.compact = static_cast<int32_t>(plan.compact);
+  p.heap_rows = static_cast<int32_t>(plan.heap_rows);
   p.gran_rows = static_cast<int32_t>(plan.gran_rows);
   p.unit_queries = static_cast<int32_t>(plan.unit_queries);
   p.ld = h->ld;

@@ -63,6 +63,10 @@ struct ScanParams {
   int32_t unit_queries;  // query rows of a unit: query_block, or 256 with pairs
   int32_t k;
   int32_t query_block;  // query rows owned per work unit (multiple of 32, <= 128)
+  // rows of the shared-memory top-k heaps and survivor buffers (<=
+  // query_block): with a single query tile, only the rows the batch has
+  // (rounded up to 8), which can leave room for another pipeline stage
+  int32_t heap_rows;
   int32_t query_tiles;
   int32_t splits;
   int32_t units;
@@ -95,6 +99,7 @@ struct Plan {
   int64_t smem_bytes, partial_bytes;
   int64_t pair = 0, gran_rows = kGranRows, unit_queries = 0;
   int64_t compact = 0;
+  int64_t heap_rows = 0;
 };
 
 // Returns 0 and fills `out`, or a KNN_E* status (KNN_EUNSUPPORTED when k is

@@ -172,13 +172,14 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, const ScanParams& p) {
   const uint32_t pad = (1024u - (base & 1023u)) & 1023u;
   s.stages = raw + pad;
   uint8_t* const heap0 = s.stages + static_cast<size_t>(p.stages) * stage_bytes(p.pair);
-  const size_t entries = static_cast<size_t>(p.k) * p.query_block;
+  const size_t entries = static_cast<size_t>(p.k) * p.heap_rows;
   s.heap = reinterpret_cast<uint64_t*>(heap0);
   s.heap_hi = reinterpret_cast<uint32_t*>(heap0);
   s.heap_lo = reinterpret_cast<uint16_t*>(s.heap_hi + entries);
-  // query_block is a multiple of 32, so the compact arrays end 8-byte aligned
+  // heap_rows is a multiple of 8, so the compact arrays end 16-byte aligned
+  // (as do the survivor buffers, ahead of the float4 norm staging)
   s.buf = p.compact ? reinterpret_cast<uint64_t*>(s.heap_lo + entries) : s.heap + entries;
-  s.norm_stage = reinterpret_cast<float*>(s.buf + static_cast<size_t>(kRowBuf) * p.query_block);
+  s.norm_stage = reinterpret_cast<float*>(s.buf + static_cast<size_t>(kRowBuf) * p.heap_rows);
   uintptr_t b = reinterpret_cast<uintptr_t>(s.norm_stage + 4 * kAccCols);
   b = (b + 7) & ~static_cast<uintptr_t>(7);
   uint64_t* bars = reinterpret_cast<uint64_t*>(b);
@@ -626,7 +627,7 @@ __device__ __noinline__ void sort_rows_cooperative(const ScanParams& p, const He
                                                    const int* sizes, int m, int s, uint32_t base,
                                                    int warp, int lane) {
   const int k = p.k;
-  const int stride = p.query_block;
+  const int stride = p.heap_rows;
   for (int r = warp - 2; r < p.query_block; r += 4) {  // warp-uniform
     const int64_t qr = static_cast<int64_t>(m) * p.unit_queries + r;
     if (qr >= p.n_queries || !in_bounds(s < p.splits, p.err)) continue;
@@ -679,7 +680,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
   const int quad = warp & 3;              // TMEM lane quadrant this warp may access
   const int row = quad * 32 + lane;       // query row within the unit's block
   const bool warp_active = quad * 32 < p.query_block;
-  const int stride = p.query_block;
+  const int stride = p.heap_rows;
   const int k = p.k;
   const float kInf = __int_as_float(0x7f800000);
   uint32_t tc = 0;
@@ -836,7 +837,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
                   float v = dv[h];
 #pragma unroll
                   for (int jj = 1; jj < kRowBuf; ++jj) v = j == jj ? dv[h + jj] : v;
-                  if (in_bounds(st.cnt < kRowBuf, p.err))
+                  if (in_bounds(st.cnt < kRowBuf && row < stride, p.err))
                     sm.buf[st.cnt * stride + row] = make_key<kMetric>(v, col0 + h + j);
                   ++st.cnt;
                   m &= m - 1u;
@@ -1187,6 +1188,7 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
                       kQueryRows * (compact ? heap_compact : heap_full);
     out->partial_bytes = n_queries * splits * k * 8;
     out->pair = 1;
+    out->heap_rows = kQueryRows;
     out->compact = compact ? 1 : 0;
     out->gran_rows = gran;
     out->unit_queries = 2 * kQueryRows;
@@ -1197,7 +1199,7 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
   // more stages (or a larger query block with as many) and every unit fits
   // them.
   struct Single {
-    int64_t qb, stages, query_tiles, splits;
+    int64_t qb, rows, stages, query_tiles, splits;
   };
   auto single = [&](int64_t per_query, Single* o) {
     int64_t qb_cap = (budget - 2 * kStageBytes) / per_query;
@@ -1206,10 +1208,13 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
     if (qb_cap < 32) return false;
     int64_t qb = ((n_queries + 31) / 32) * 32;
     if (qb > qb_cap) qb = qb_cap;
-    int64_t stages = (budget - qb * per_query) / kStageBytes;
+    // a single query tile needs heaps only for the rows the batch has
+    const int64_t rows = n_queries <= qb ? (n_queries + 7) / 8 * 8 : qb;
+    int64_t stages = (budget - rows * per_query) / kStageBytes;
     if (stages > kMaxStages) stages = kMaxStages;
     if (stages < 2) return false;
     o->qb = qb;
+    o->rows = rows;
     o->stages = stages;
     o->query_tiles = (n_queries + qb - 1) / qb;
     o->splits = pick_splits(o->query_tiles, (n_rows + kGranRows - 1) / kGranRows, kGranRows,
@@ -1233,7 +1238,9 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
   out->units = units;
   out->grid = units < num_sms ? units : num_sms;
   out->stages = c.stages;
-  out->smem_bytes = kSmemReserve + c.stages * kStageBytes + c.qb * (cmp_ok ? heap_compact : heap_full);
+  out->smem_bytes =
+      kSmemReserve + c.stages * kStageBytes + c.rows * (cmp_ok ? heap_compact : heap_full);
+  out->heap_rows = c.rows;
   out->partial_bytes = n_queries * c.splits * k * 8;
   out->pair = 0;
   out->compact = cmp_ok ? 1 : 0;
@@ -1277,6 +1284,8 @@ cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
   if (p.n_gran != (p.n_rows + p.gran_rows - 1) / p.gran_rows || p.splits < 1 ||
       p.splits > p.n_gran || (p.pair != 0) != (plan.pair != 0) ||
       (p.compact != 0) != (plan.compact != 0) || (p.compact && !compact_ok) ||
+      p.heap_rows != plan.heap_rows || p.heap_rows <= 0 || p.heap_rows > p.query_block ||
+      p.heap_rows % 8 != 0 ||
       (p.pair && (plan.grid % 2 != 0 || p.gran_rows != 2 * kGranRows ||
                   p.unit_queries != 2 * kQueryRows || p.query_block != kQueryRows)))
     return cudaErrorInvalidValue;

@@ -85,10 +85,15 @@ def test_planner_compact_heaps(engine):
     assert c4["pair"] == 1 and c4["compact_heap"] == 1 and c4["stages"] == 4
     big = engine.plan_search(10_000_000, 1024, 10_000, 100)
     assert big["pair"] == 1 and big["compact_heap"] == 0 and big["stages"] == 3
-    single = engine.plan_search(1_000_000, 1024, 100, 64)
+    single = engine.plan_search(1_000_000, 1024, 128, 64)
     assert single["pair"] == 0 and single["compact_heap"] == 1 and single["stages"] == 3
+    # a single query tile keeps heaps only for the batch's rows (104 of 128
+    # at Q = 100), which leaves room for a third stage at K = 100
+    q100 = engine.plan_search(1_000_000, 1024, 100, 100)
+    assert q100["pair"] == 0 and q100["stages"] == 3 and q100["smem_bytes"] <= 232448
     assert engine.plan_search(1_000_000, 1024, 100, 10)["compact_heap"] == 0
-    assert engine.plan_search(1_000_000, 1024, 16, 256)["compact_heap"] == 0
+    c5 = engine.plan_search(1_000_000, 1024, 16, 256)  # heaps for 16 rows: 4 stages
+    assert c5["compact_heap"] == 1 and c5["stages"] == 4
 
 
 def test_planner_limits(engine):
