@@ -555,7 +555,8 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
   if (rerank) KNN_CUDA(cudaMemsetAsync(h->uncert_dev, 0, sizeof(int), h->stream));
   KNN_CUDA(knn::launch_convert_rows(qsrc, false, nq, nq_pad, h->dim, h->q16.as<__half>(),
                                     h->ld, h->qnorm.as<float>(), h->stream,
-                                    h->bound.as<uint32_t>(), nq, h->epoch_dev));
+                                    h->bound.as<uint32_t>(), nq, h->epoch_dev,
+                                    plan.spread != 0));
   CUtensorMap qmap;
   if ((st = encode_rows(&qmap, h->q16.as<__half>(), nq_pad, h->ld, knn::kQueryRows)) != KNN_OK)
     return st;
@@ -573,6 +574,7 @@ int enqueue_pipeline(knn_index* h, const float* qsrc, int64_t nq, int64_t k, int
   p.pair = static_cast<int32_t>(plan.pair);
   p.compact = static_cast<int32_t>(plan.compact);
   p.heap_rows = static_cast<int32_t>(plan.heap_rows);
+  p.spread = static_cast<int32_t>(plan.spread);
   p.gran_rows = static_cast<int32_t>(plan.gran_rows);
   p.unit_queries = static_cast<int32_t>(plan.unit_queries);
   p.ld = h->ld;
@@ -1779,7 +1781,7 @@ int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
     qsrc = q32;
   }
   KNN_CUDA(knn::launch_convert_rows(qsrc, false, nq, nq_pad, h->dim, q16, h->ld, qnorm,
-                                    h->stream));
+                                    h->stream, nullptr, 0, nullptr, plan.spread != 0));
   CUtensorMap qmap;
   if ((st = encode_rows(&qmap, q16, nq_pad, h->ld, knn::kQueryRows)) != KNN_OK) return st;
 
@@ -1796,6 +1798,7 @@ int noalloc_search(knn_index* h, const float* queries, int64_t nq, int64_t k,
   p.pair = static_cast<int32_t>(plan.pair);
   p.compact = static_cast<int32_t>(plan.compact);
   p.heap_rows = static_cast<int32_t>(plan.heap_rows);
+  p.spread = static_cast<int32_t>(plan.spread);
   p.gran_rows = static_cast<int32_t>(plan.gran_rows);
   p.unit_queries = static_cast<int32_t>(plan.unit_queries);
   p.ld = h->ld;

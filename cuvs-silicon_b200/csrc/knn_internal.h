@@ -67,6 +67,10 @@ struct ScanParams {
   // query_block): with a single query tile, only the rows the batch has
   // (rounded up to 8), which can leave room for another pipeline stage
   int32_t heap_rows;
+  // spread = 1: 32-query blocks in the spread layout (spread_query_row):
+  // block m's slab starts at query row 128 * m and query j of the block is
+  // TMEM lane 32 * (j % 4) + j / 4
+  int32_t spread;
   int32_t query_tiles;
   int32_t splits;
   int32_t units;
@@ -100,6 +104,7 @@ struct Plan {
   int64_t pair = 0, gran_rows = kGranRows, unit_queries = 0;
   int64_t compact = 0;
   int64_t heap_rows = 0;
+  int64_t spread = 0;
 };
 
 // Returns 0 and fills `out`, or a KNN_E* status (KNN_EUNSUPPORTED when k is
@@ -130,12 +135,23 @@ cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
 cudaError_t launch_convert_rows(const void* in, bool in_is_half, int64_t rows,
                                 int64_t rows_out, int64_t dim, __half* out, int64_t ld,
                                 float* norms, cudaStream_t stream, uint32_t* fill = nullptr,
-                                int64_t fill_n = 0, uint32_t* epoch = nullptr);
+                                int64_t fill_n = 0, uint32_t* epoch = nullptr,
+                                bool spread = false);
+
+// Spread query blocks (ScanParams::spread): query j of a 32-query block
+// sits in row 32 * (j % 4) + j / 4 of the block's 128-row slab, so each of
+// the 4 TMEM lane quadrants (one epilogue warp each) holds up to 8 of them.
+// launch_convert_rows(..., spread = true) writes that layout (the slab of
+// block m starts at row 128 * m; rows holding no query are zeros).
+inline int64_t spread_query_row(int64_t q) {
+  return q / 32 * kQueryRows + 32 * (q % 4) + (q % 32) / 4;
+}
 
 // Rows of the fp16 query buffer a search needs: every 128-row query slab
 // the scan kernel loads lies inside it, so no TMA box leaves the buffer.
 inline int64_t padded_query_rows(const Plan& plan) {
   if (plan.pair) return plan.query_tiles * 2 * kQueryRows;
+  if (plan.spread) return plan.query_tiles * kQueryRows;
   return (plan.query_tiles - 1) * plan.query_block + kQueryRows;
 }
 

@@ -39,7 +39,7 @@ __global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, i
                                     int64_t dim, __half* __restrict__ out, int64_t ld,
                                     float* __restrict__ norms, bool vec,
                                     uint32_t* __restrict__ fill, int64_t fill_n,
-                                    uint32_t* __restrict__ epoch) {
+                                    uint32_t* __restrict__ epoch, bool spread) {
   // Let the next kernel (the scan) be scheduled now: its dataset loads do
   // not depend on this kernel, and it waits before reading the queries.
   // This kernel is itself a programmatic dependent of the previous search's
@@ -60,7 +60,13 @@ __global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, i
   for (int64_t r = first; r < rows_out; r += step) {
     float acc = 0.0f;
     __half* orow = out + r * ld;
-    if (r >= rows) {
+    // the input row this output row holds (spread: see spread_query_row)
+    int64_t src = r;
+    if (spread) {
+      const int64_t lr = r % kQueryRows, l = lr % 32;
+      src = l < 8 ? r / kQueryRows * 32 + 4 * l + lr / 32 : rows;
+    }
+    if (src >= rows) {
       // padding row: zeros (keeps whole TMA boxes inside the allocation)
       for (int64_t c = lane; c < ld; c += 32) orow[c] = __float2half_rn(0.0f);
     } else if (vec) {
@@ -69,7 +75,7 @@ __global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, i
         float v[8];
         if constexpr (kHalfIn) {
           const uint4 raw = reinterpret_cast<const uint4*>(static_cast<const __half*>(in) +
-                                                           r * dim)[g];
+                                                           src * dim)[g];
           const __half2* h = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -78,10 +84,10 @@ __global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, i
             v[2 * j + 1] = f.y;
           }
         } else {
-          const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(in) +
-                                                              r * dim) + 2 * g;
-          const float4 a = src[0];
-          const float4 b = src[1];
+          const float4* f4 = reinterpret_cast<const float4*>(static_cast<const float*>(in) +
+                                                             src * dim) + 2 * g;
+          const float4 a = f4[0];
+          const float4 b = f4[1];
           v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
           v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
         }
@@ -103,7 +109,7 @@ __global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, i
       for (int64_t c = lane; c < ld; c += 32) {
         __half h = __float2half_rn(0.0f);
         if (c < dim) {
-          h = __float2half_rn(load_elem<kHalfIn>(in, r * dim + c));
+          h = __float2half_rn(load_elem<kHalfIn>(in, src * dim + c));
           const float f = __half2float(h);
           acc = fmaf(f, f, acc);
         }
@@ -112,7 +118,7 @@ __global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, i
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane == 0 && r < rows) norms[r] = acc;
+    if (lane == 0 && src < rows) norms[src] = acc;
   }
 }
 
@@ -121,7 +127,7 @@ __global__ void convert_rows_kernel(const void* __restrict__ in, int64_t rows, i
 cudaError_t launch_convert_rows(const void* in, bool in_is_half, int64_t rows, int64_t rows_out,
                                 int64_t dim, __half* out, int64_t ld, float* norms,
                                 cudaStream_t stream, uint32_t* fill, int64_t fill_n,
-                                uint32_t* epoch) {
+                                uint32_t* epoch, bool spread) {
   if (rows_out < rows) rows_out = rows;
   if (rows_out <= 0) return cudaSuccess;
   const bool vec = (dim % 8 == 0) && ((reinterpret_cast<uintptr_t>(in) & 15u) == 0) &&
@@ -141,9 +147,9 @@ cudaError_t launch_convert_rows(const void* in, bool in_is_half, int64_t rows, i
   cfg.numAttrs = 1;
   if (in_is_half)
     return cudaLaunchKernelEx(&cfg, convert_rows_kernel<true>, in, rows, rows_out, dim, out, ld,
-                              norms, vec, fill, fill ? fill_n : int64_t(0), epoch);
+                              norms, vec, fill, fill ? fill_n : int64_t(0), epoch, spread);
   return cudaLaunchKernelEx(&cfg, convert_rows_kernel<false>, in, rows, rows_out, dim, out, ld,
-                            norms, vec, fill, fill ? fill_n : int64_t(0), epoch);
+                            norms, vec, fill, fill ? fill_n : int64_t(0), epoch, spread);
 }
 
 }  // namespace knn

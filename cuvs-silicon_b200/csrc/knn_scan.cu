@@ -300,7 +300,9 @@ __device__ void producer(const CUtensorMap* qmap, const CUtensorMap* xmap,
   bool failed = false;
   for (int u = first; u < p.units && !failed; u += step) {
     const Unit un = unit_of(p, u);
-    const int32_t qy = un.m * p.unit_queries + static_cast<int32_t>(crank) * kQueryRows;
+    // the unit's 128-row query slab (a spread block's slab is its own)
+    const int32_t qy = p.spread ? un.m * kQueryRows
+                                : un.m * p.unit_queries + static_cast<int32_t>(crank) * kQueryRows;
     if (!in_bounds(qy >= 0 && qy + kQueryRows <= p.q_rows, p.err)) {
       failed = true;
       break;
@@ -622,16 +624,26 @@ __device__ __forceinline__ void write_sorted_row(const HeapStore<kC>& heap, int 
 // The unit lists of a 32-row query block, row r sorted and written by
 // epilogue warp r % 4 (write_sorted_row).  Kept out of line so that its
 // registers do not weigh on the epilogue's tile loop.
+// Heap size of slot r (r < 32) of a 32-query block, as its owner left it in
+// its own norm-staging slice (warp w's slice is w - 2; the warp of TMEM lane
+// quadrant c is (c + 2) & 3 slices in): slot r is lane r of quadrant 0, or
+// in a spread block lane r / 4 of quadrant r % 4.
+__device__ __forceinline__ int heap_size_of(const float* norm_stage, int r, bool spread) {
+  const int quad = spread ? r % 4 : 0;
+  const int lane = spread ? r / 4 : r;
+  return reinterpret_cast<const int*>(norm_stage + ((quad + 2) & 3) * kAccCols)[lane];
+}
+
 template <int kMetric, bool kC>
 __device__ __noinline__ void sort_rows_cooperative(const ScanParams& p, const HeapStore<kC> heap,
-                                                   const int* sizes, int m, int s, uint32_t base,
-                                                   int warp, int lane) {
+                                                   const float* norm_stage, int m, int s,
+                                                   uint32_t base, int warp, int lane) {
   const int k = p.k;
   const int stride = p.heap_rows;
   for (int r = warp - 2; r < p.query_block; r += 4) {  // warp-uniform
     const int64_t qr = static_cast<int64_t>(m) * p.unit_queries + r;
     if (qr >= p.n_queries || !in_bounds(s < p.splits, p.err)) continue;
-    const int n = sizes[r];
+    const int n = heap_size_of(norm_stage, r, p.spread != 0);
     if (!in_bounds(n >= 0 && n <= k && r < stride, p.err)) continue;
     float* od = p.part_d + (static_cast<size_t>(qr) * p.splits + s) * k;
     uint32_t* oi = p.part_i + (static_cast<size_t>(qr) * p.splits + s) * k;
@@ -678,8 +690,12 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
   const int first = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int step = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
   const int quad = warp & 3;              // TMEM lane quadrant this warp may access
-  const int row = quad * 32 + lane;       // query row within the unit's block
-  const bool warp_active = quad * 32 < p.query_block;
+  const int row = quad * 32 + lane;       // TMEM lane = row of the query slab
+  // the row's query within the unit's block, which also indexes its heap and
+  // survivor buffer: the row itself, or in a spread block query 4 * lane +
+  // quad for lanes 0-7 (other lanes hold none: slot >= query_block)
+  const int slot = p.spread ? (lane < 8 ? 4 * lane + quad : p.query_block + lane) : row;
+  const bool warp_active = p.spread || quad * 32 < p.query_block;
   const int stride = p.heap_rows;
   const int k = p.k;
   const float kInf = __int_as_float(0x7f800000);
@@ -693,8 +709,8 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
     // narrower last tile) accumulator columns the tile's MMAs did not write
     const int64_t row_lim = un.r_end < p.n_rows ? un.r_end : p.n_rows;
     const int64_t q = static_cast<int64_t>(un.m) * p.unit_queries +
-                      static_cast<int64_t>(crank) * kQueryRows + row;
-    const bool valid_q = warp_active && row < p.query_block && q < p.n_queries;
+                      static_cast<int64_t>(crank) * kQueryRows + slot;
+    const bool valid_q = warp_active && slot < p.query_block && q < p.n_queries;
     const float qn = valid_q ? p.query_norms[q] : 0.0f;
     RowState<kReg> st;
     st.thr = valid_q ? (p.thr_init ? p.thr_init[q] : kInf) : __int_as_float(0xff800000);
@@ -823,7 +839,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
             for (int j = 0; j < kRowBuf; ++j) mask |= (dv[h + j] < st.thr ? 1u : 0u) << j;
             if (__any_sync(0xffffffffu, mask != 0)) {
               if (__any_sync(0xffffffffu, st.cnt + __popc(mask) > kRowBuf)) {
-                flush_buffer<kMetric, kReg, kC>(st, sm, k, stride, row, base, p.err);
+                flush_buffer<kMetric, kReg, kC>(st, sm, k, stride, slot, base, p.err);
                 mask = 0;
 #pragma unroll
                 for (int j = 0; j < kRowBuf; ++j) mask |= (dv[h + j] < st.thr ? 1u : 0u) << j;
@@ -837,8 +853,8 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
                   float v = dv[h];
 #pragma unroll
                   for (int jj = 1; jj < kRowBuf; ++jj) v = j == jj ? dv[h + jj] : v;
-                  if (in_bounds(st.cnt < kRowBuf && row < stride, p.err))
-                    sm.buf[st.cnt * stride + row] = make_key<kMetric>(v, col0 + h + j);
+                  if (in_bounds(st.cnt < kRowBuf && slot < stride, p.err))
+                    sm.buf[st.cnt * stride + slot] = make_key<kMetric>(v, col0 + h + j);
                   ++st.cnt;
                   m &= m - 1u;
                 }
@@ -879,7 +895,7 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
       // survivors enter the heap at every tile end so thr tightens early (the
       // accumulator is already released; this overlaps the next tile's MMAs)
       if (warp_active && __any_sync(0xffffffffu, st.cnt > 0)) {
-        flush_buffer<kMetric, kReg, kC>(st, sm, k, stride, row, base, p.err);
+        flush_buffer<kMetric, kReg, kC>(st, sm, k, stride, slot, base, p.err);
         if (p.bound && valid_q && st.root != empty_key<kMetric>()) {
           const uint32_t bits = dist_order_bits(key_dist<kMetric>(st.root));
           if (bits < st.pub && in_bounds(q < p.n_queries, p.err)) {
@@ -891,11 +907,12 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
     }
     if (failed) break;
     if (p.pilot) continue;
-    if (warp_active) flush_buffer<kMetric, kReg, kC>(st, sm, k, stride, row, base, p.err);
+    if (warp_active) flush_buffer<kMetric, kReg, kC>(st, sm, k, stride, slot, base, p.err);
     if (!kReg && p.query_block == kGranRows) {  // grid-uniform
-      // Query blocks of 32 rows: one warp owns every row and would sort
-      // each row's heap alone, lane by lane (a 256-entry heap sort costs
-      // tens of microseconds at the end of the unit).  Each owner leaves
+      // Query blocks of 32 rows: one warp owns every row (up to 8 per warp
+      // in a spread block) and would sort each row's heap alone, lane by
+      // lane (a 256-entry heap sort costs tens of microseconds at the end
+      // of the unit).  Each owner leaves
       // its row's heap size in its own norm-staging slice (free until its
       // next tile); once the warps have met, all of them read the sizes,
       // and if some heap holds kCoopMinHeap entries or more, row r is
@@ -908,11 +925,11 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
         failed = true;
         break;
       }
-      // rows 0-31 belong to TMEM lane quadrant 0, the warp of slice 2
-      const int* sizes = reinterpret_cast<const int*>(sm.norm_stage + 2 * kAccCols);
-      const bool coop = __reduce_max_sync(0xffffffffu, sizes[lane]) >= kCoopMinHeap;
+      const bool coop =
+          __reduce_max_sync(0xffffffffu, heap_size_of(sm.norm_stage, lane, p.spread != 0)) >=
+          kCoopMinHeap;
       if (coop)
-        sort_rows_cooperative<kMetric, kC>(p, heap_of<kC>(sm), sizes, un.m, u / p.query_tiles,
+        sort_rows_cooperative<kMetric, kC>(p, heap_of<kC>(sm), sm.norm_stage, un.m, u / p.query_tiles,
                                            base, warp, lane);
       if (!epilogue_meet(sm, meets, lane, p.err)) {
         failed = true;
@@ -940,16 +957,16 @@ __device__ void epilogue(const ScanParams& p, const Smem& sm, uint32_t tmem_base
       const HeapStore<kC> heap = heap_of<kC>(sm);
       const int n = st.size;
       for (int end = n - 1; end > 0; --end) {
-        const uint64_t top = heap.get(row);
-        const uint64_t last = heap.get(end * stride + row);
-        heap.set(end * stride + row, top);
-        heap_sift_down(heap, end, stride, row, 0, last, k, p.err);
+        const uint64_t top = heap.get(slot);
+        const uint64_t last = heap.get(end * stride + slot);
+        heap.set(end * stride + slot, top);
+        heap_sift_down(heap, end, stride, slot, 0, last, k, p.err);
       }
       const int s = u / p.query_tiles;
       float* od = p.part_d + (static_cast<size_t>(q) * p.splits + s) * k;
       uint32_t* oi = p.part_i + (static_cast<size_t>(q) * p.splits + s) * k;
       for (int r = 0; r < k; ++r) {
-        const uint64_t key = r < n ? heap.get(r * stride + row) : empty_key<kMetric>();
+        const uint64_t key = r < n ? heap.get(r * stride + slot) : empty_key<kMetric>();
         od[r] = key_dist<kMetric>(key);
         oi[r] = r < n && kC ? base + static_cast<uint32_t>(key) : static_cast<uint32_t>(key);
       }
@@ -1241,6 +1258,9 @@ int plan_search(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k, int n
   out->smem_bytes =
       kSmemReserve + c.stages * kStageBytes + c.rows * (cmp_ok ? heap_compact : heap_full);
   out->heap_rows = c.rows;
+  // 32-query blocks with shared-memory heaps spread their queries over the
+  // 4 epilogue warps (spread_query_row)
+  out->spread = (c.qb == kGranRows && k > kRegK) ? 1 : 0;
   out->partial_bytes = n_queries * c.splits * k * 8;
   out->pair = 0;
   out->compact = cmp_ok ? 1 : 0;
@@ -1285,7 +1305,9 @@ cudaError_t launch_scan(const CUtensorMap& qmap, const CUtensorMap& xmap,
       p.splits > p.n_gran || (p.pair != 0) != (plan.pair != 0) ||
       (p.compact != 0) != (plan.compact != 0) || (p.compact && !compact_ok) ||
       p.heap_rows != plan.heap_rows || p.heap_rows <= 0 || p.heap_rows > p.query_block ||
-      p.heap_rows % 8 != 0 ||
+      p.heap_rows % 8 != 0 || p.spread != plan.spread ||
+      (p.spread && (p.pair || p.query_block != kGranRows || p.k <= kRegK ||
+                    p.q_rows < static_cast<int64_t>(p.query_tiles) * kQueryRows)) ||
       (p.pair && (plan.grid % 2 != 0 || p.gran_rows != 2 * kGranRows ||
                   p.unit_queries != 2 * kQueryRows || p.query_block != kQueryRows)))
     return cudaErrorInvalidValue;

@@ -141,6 +141,10 @@ SHAPES = [
     # register top-k, several pair tiles, and the pilot pass at k = 32
     (20011, 64, 1000, 16),
     (1000, 128, 200, 32),
+    # 32-query blocks spread over the four TMEM lane quadrants (k > 16):
+    # a ragged single block, and two blocks the second of which holds 5
+    (3001, 128, 29, 100),
+    (2000, 64, 37, 256),
 ]
 
 
