@@ -48,6 +48,8 @@ constexpr int kRankPlaceMax = 1024;  // candidates ordered by rank counting (4 p
 // (it is quadratic; the block-wide sort takes over above).
 constexpr int kLongList = 128;
 constexpr int kRankPlaceLong = 256;
+// Entries per list in the fallback threshold sample (see merge_query).
+constexpr int kSampleJ = 8;
 static_assert(kSelCap + kCandCap <= kStageEntries, "threshold arrays share the stage");
 
 __device__ __forceinline__ bool less_pair(float da, uint32_t ia, float db, uint32_t ib) {
@@ -188,6 +190,11 @@ __device__ __forceinline__ void block_sort(float* d, uint32_t* i, int p2) {
 __device__ __forceinline__ uint32_t order_key(float d) {
   const uint32_t u = __float_as_uint(d == 0.0f ? 0.0f : d);
   return u ^ ((u >> 31) ? 0xFFFFFFFFu : 0x80000000u);
+}
+
+// Inverse of order_key.
+__device__ __forceinline__ float key_float(uint32_t b) {
+  return __uint_as_float(b ^ ((b >> 31) ? 0x80000000u : 0xFFFFFFFFu));
 }
 
 // The image (order_key) of the k-th smallest of d[0..n), 1 <= k <= n, by a
@@ -422,6 +429,8 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
   float* sd = reinterpret_cast<float*>(smem_raw);
   uint32_t* si = reinterpret_cast<uint32_t*>(sd + kStageEntries);
   __shared__ int s_count;
+  __shared__ int s_hist[kMergeWarps * 32];  // radix selects
+  __shared__ int s_misc[10];
 
   const int64_t q = blockIdx.x;
   const int tid = threadIdx.x;
@@ -484,6 +493,32 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
     block_sort(seld, seli, p2);
     td = seld[r - 1];
     ti = seli[r - 1];
+  }
+
+  // Fewer than r lists hold j entries (the scan's shared bound leaves many
+  // unit lists short), so tau is the padding.  The first kSampleJ entries
+  // of every list then give a bound instead: if at least k of them are
+  // valid, their k-th smallest distance D has k entries at or below it, so
+  // (D, any index) bounds the merged k-th entry; with short lists D is
+  // close to it.  (Without this, thousands of candidates went to the fold.)
+  if (ti == kNoIndex && n_lists * kSampleJ <= kSelCap && k <= n_lists * kSampleJ) {
+    __syncthreads();  // every thread has read tau from the selection array
+    const int ns = n_lists * kSampleJ;
+    for (int e = tid; e < ns; e += blockDim.x) {
+      const int l = e / kSampleJ, rr = e - l * kSampleJ;
+      float dv = kInf;
+      if (rr < k) {
+        const int64_t at = static_cast<int64_t>(l) * stride_list + rr;
+        if (qi[at] != kNoIndex) dv = qd[at];
+      }
+      seld[e] = dv;
+    }
+    __syncthreads();
+    const uint32_t kth = block_select_kth(seld, ns, k, s_hist, s_misc);
+    if (kth != order_key(kInf)) {
+      td = key_float(kth);
+      ti = kNoIndex - 1u;  // every entry at distance D is kept
+    }
   }
 
   // candidates: every valid entry (d, i) <= tau (every valid entry when
@@ -658,8 +693,6 @@ __device__ __forceinline__ void merge_query(const float* __restrict__ in_d,
     // With ~3,800 candidates (tau the padding) a traced search spent 88 to
     // 160 us per query block in the 4096-entry sort; with the select the
     // whole search (125k rows, Q = 16, K = 256) went 130.7 -> 116.1 us.
-    __shared__ int s_hist[kMergeWarps * 32];
-    __shared__ int s_misc[10];
     const uint32_t kth = block_select_kth(cd, count, k, s_hist, s_misc);
     if (tid == 0) s_count = 0;
     __syncthreads();

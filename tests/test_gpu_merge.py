@@ -41,6 +41,8 @@ def make_lists(rng, n_lists, nq, k, pattern, negative=False):
                 n = int(rng.integers(0, 8))
             elif pattern == "shortish":
                 n = int(rng.integers(0, 40))
+            elif pattern == "mixed":  # mostly short lists, every third long
+                n = int(rng.integers(40, k + 1)) if l % 3 == 0 else int(rng.integers(0, 4))
             else:  # ties: few distinct distances
                 n = int(rng.integers(k // 2, k + 1))
             if pattern == "ties":
@@ -67,6 +69,12 @@ CASES = [
     (8, 7, 10, "ties", False),
     (148, 2, 256, "short", True),
     (24, 3, 200, "ties", True),
+    # too few lists hold j entries for a threshold: the first 8 entries of
+    # every list bound the k-th instead (exact when the lists are short,
+    # loose when some are long)
+    (148, 3, 256, "mixed", False),
+    (148, 3, 100, "mixed", True),
+    (200, 2, 64, "mixed", False),
 ]
 
 
