@@ -27,10 +27,21 @@
 // same number of rows to within one granule: a unit is a run of full
 // 256-row tiles and one narrower last tile (its MMAs use N = its width and
 // its rows arrive as 32-row TMA boxes).  A persistent CTA walks units
-// blockIdx.x, +gridDim.x, ...; at the end of a unit each query's heap is
-// sorted and written as list s of that query: part[(q * splits + s) * k + r].  The merge kernel (knn_merge.cu)
-// reduces the lists to the final top-k, ordered by (distance, index) like
+// blockIdx.x, +gridDim.x, ...; at the end of a unit each query's top-k is
+// sorted and written as list s of that query:
+// part[(q * splits + s) * k + r].  The merge kernel (knn_merge.cu) reduces
+// the lists to the final top-k, ordered by (distance, index) like
 // src/cagra.cpp:229-238.
+//
+// Variants chosen by plan_search (same results, different speed):
+//   * CTA pairs (kPair): clusters of two CTAs issue cta_group::2 MMAs with
+//     M = 256, each CTA loading its 128 queries and half of every dataset
+//     tile, for more than 128 queries;
+//   * register top-k (kReg, k <= 16), shared-memory heaps of 8-byte keys,
+//     or compact heaps of 6-byte entries (kC);
+//   * spread 32-query blocks (ScanParams::spread): the queries sit in all
+//     four TMEM lane quadrants, so every epilogue warp owns some;
+//   * heaps sized to the batch's rows when there is one query tile.
 //
 // Every TMA load lands in the issuing CTA only (the same code runs under multi-GPU
 // sharding).  Every mbarrier wait is bounded (ptx.cuh).
